@@ -1,0 +1,581 @@
+/*
+ * pkv_oracle.c -- CPU restatement of the Pyramid Forcing MegaCache hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker the CUDA kernels of the
+ * product are compared against; it is loaded (through oracle/pkv_oracle.py)
+ * only by tests/, by __graft_entry__.smoke() and by bench.py's cpu_baseline
+ * leg.  Nothing in the product path links, loads or calls it.
+ *
+ * Every function restates one piece of the reference and names the file:line
+ * it follows (paths relative to the reference project root):
+ *
+ *   orc_state_update  pyramidkv/csrc/anchor_store_update.cu:43-313
+ *                     (Python mirror pyramidkv/_mega_state_ref.py:116-333)
+ *   orc_map_sink_time pyramidkv/csrc/mega_plan.cc:63-80 (rope.py:86-101)
+ *   orc_plan_multi    pyramidkv/csrc/mega_plan.cc:133-264 and :510-654
+ *   orc_layer_offset  pyramidkv/_mega_attention.py:349-385
+ *   orc_update_frames pyramidkv/csrc/pyramidkv_update.cu:21-110
+ *   orc_merge_accum   pyramidkv/csrc/mega_merge_accum.cu:52-252
+ *   orc_pack          pyramidkv/csrc/pyramidkv_pack.cu:28-185
+ *
+ * The PerHeadState layout is declared here independently of the product's
+ * header (pyramidkv/csrc/anchor_store.cuh:62-132 is the layout both follow);
+ * its 600-byte size and field offsets are pinned by tests against the
+ * reference's numpy mirror (pyramidkv/_mega_state_ops.py:36-77).
+ *
+ * bf16 values travel as uint16_t bit patterns.  bf16 -> f32 is exact; f32 ->
+ * bf16 is round-to-nearest-even (what __float2bfloat16 does for finite input).
+ *
+ * Floating-point rounding of the RoPE rotation: the reference's kernel is
+ * compiled with nvcc's default FMA contraction, so `kr*fr - ki*fi` may be
+ * evaluated as one product rounded and one fused.  orc_pack takes a
+ * `rope_mode` selecting the evaluation order (see ORC_ROPE_*) so the oracle
+ * can reproduce whichever order the compiled reference uses; the GPU tests
+ * pin the mode against the reference's own kernel.
+ */
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- bounds (anchor_store.cuh:39-45,148) ------------------------------- */
+#define O_MAX_PHASE 6
+#define O_MAX_BUCKET 4
+#define O_MAX_TKEYED 24
+#define O_MAX_LAG 4
+#define O_MAX_MERGE_BLOCKS 6
+#define O_MAX_MERGE_ACTIVE 2
+#define O_MAX_MERGE_BLOCK_FRAMES 4
+#define O_MAX_MERGE_TOKENS 420
+
+enum { O_SK_RECENT = 0, O_SK_CYCLIC = 1, O_SK_STRIDE = 2, O_SK_LAG = 3, O_SK_MERGE = 4 };
+enum { O_DST_SKIP = -1, O_DST_SINK = 0, O_DST_MIDDLE = 1, O_DST_RECENT = 2,
+       O_DST_MERGE_ACCUM = 5 };
+
+typedef struct {
+    int8_t  kind;
+    int8_t  sink_capacity;
+    int8_t  pad0[2];
+    int32_t period, bucket_cap, interval, capacity, patch_size, block_frames;
+    int32_t lag_offsets[O_MAX_LAG];
+    int32_t lag_offset_count;
+    int32_t cyclic_slot[O_MAX_PHASE * O_MAX_BUCKET];
+    int32_t cyclic_t[O_MAX_PHASE * O_MAX_BUCKET];
+    int8_t  cyclic_cursor[O_MAX_PHASE];
+    int32_t tkey_slot[O_MAX_TKEYED];
+    int32_t tkey_t[O_MAX_TKEYED];
+    int8_t  tkey_count, tkey_head;
+    int8_t  pad1[2];
+    int32_t mc_slot[O_MAX_MERGE_BLOCKS];
+    int32_t mc_block_id[O_MAX_MERGE_BLOCKS];
+    int32_t mc_start_t[O_MAX_MERGE_BLOCKS];
+    int32_t mc_end_t[O_MAX_MERGE_BLOCKS];
+    int32_t mc_median_t[O_MAX_MERGE_BLOCKS];
+    int8_t  mc_count;
+    int8_t  pad2[3];
+    int32_t ma_block_id[O_MAX_MERGE_ACTIVE];
+    int32_t ma_slot[O_MAX_MERGE_ACTIVE];
+    int8_t  ma_seen[O_MAX_MERGE_ACTIVE][O_MAX_MERGE_BLOCK_FRAMES];
+    int8_t  ma_complete[O_MAX_MERGE_ACTIVE];
+    int8_t  pad3[2];
+    int32_t cached_num_groups;
+} OrcState;
+
+_Static_assert(sizeof(OrcState) == 600, "PerHeadState restatement must be 600 bytes");
+
+int64_t orc_state_size(void) { return (int64_t)sizeof(OrcState); }
+
+/* Field offsets, so the Python side can check them against the reference's
+ * numpy structured dtype. */
+int64_t orc_state_offset(int which) {
+    switch (which) {
+    case 0: return (int64_t)offsetof(OrcState, cyclic_cursor);
+    case 1: return (int64_t)offsetof(OrcState, tkey_slot);
+    case 2: return (int64_t)offsetof(OrcState, tkey_count);
+    case 3: return (int64_t)offsetof(OrcState, mc_slot);
+    case 4: return (int64_t)offsetof(OrcState, mc_count);
+    case 5: return (int64_t)offsetof(OrcState, ma_block_id);
+    case 6: return (int64_t)offsetof(OrcState, ma_seen);
+    case 7: return (int64_t)offsetof(OrcState, cached_num_groups);
+    default: return -1;
+    }
+}
+
+/* ---- bf16 helpers -------------------------------------------------------- */
+static inline float bf2f(uint16_t b) {
+    uint32_t u = ((uint32_t)b) << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static inline uint16_t f2bf(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) {
+        return (uint16_t)((u >> 16) | 0x40); /* quiet NaN */
+    }
+    uint32_t lsb = (u >> 16) & 1u;
+    u += 0x7fffu + lsb;
+    return (uint16_t)(u >> 16);
+}
+
+uint16_t orc_f32_to_bf16(float f) { return f2bf(f); }
+
+/* ======================================================================== */
+/* State machine: anchor_store_update.cu:43-231 (update_*), :233-313 (kernel) */
+/* ======================================================================== */
+typedef struct {
+    int32_t kind, slot, accum_slot, local_idx, finalize_idx, is_new;
+} OrcDesc;
+
+static void st_cyclic(OrcState *s, int32_t t, OrcDesc *d) {
+    /* anchor_store_update.cu:43-61 */
+    int32_t phase = t % s->period;
+    int32_t cursor = s->cyclic_cursor[phase];
+    int32_t slot = phase * s->bucket_cap + cursor;
+    s->cyclic_slot[slot] = slot;
+    s->cyclic_t[slot] = t;
+    s->cyclic_cursor[phase] = (int8_t)((cursor + 1) % s->bucket_cap);
+    d->kind = O_DST_MIDDLE;
+    d->slot = slot;
+}
+
+static void st_tkeyed(OrcState *s, int32_t t, OrcDesc *d, int stride_filter) {
+    /* stride: anchor_store_update.cu:63-89; lag: :91-109 */
+    if (stride_filter && (t % s->interval) != 0) {
+        d->kind = O_DST_SKIP;
+        d->slot = -1;
+        return;
+    }
+    int32_t slot = (int32_t)s->tkey_head;
+    s->tkey_head = (int8_t)((slot + 1) % s->capacity);
+    if (s->tkey_count < s->capacity) s->tkey_count = (int8_t)(s->tkey_count + 1);
+    s->tkey_slot[slot] = slot;
+    s->tkey_t[slot] = t;
+    d->kind = O_DST_MIDDLE;
+    d->slot = slot;
+}
+
+static void clear_active(OrcState *s, int a) {
+    s->ma_block_id[a] = -1;
+    for (int j = 0; j < O_MAX_MERGE_BLOCK_FRAMES; ++j) s->ma_seen[a][j] = 0;
+    s->ma_complete[a] = 0;
+}
+
+static void st_merge(OrcState *s, int32_t t, OrcDesc *d) {
+    /* anchor_store_update.cu:120-231 */
+    d->kind = O_DST_SKIP; d->slot = -1; d->accum_slot = -1; d->local_idx = -1;
+    d->finalize_idx = -1; d->is_new = 0;
+    if (s->block_frames <= 0) return;
+    int32_t block_id = t / s->block_frames;
+    int32_t local_idx = t % s->block_frames;
+
+    int32_t a = -1;
+    for (int i = 0; i < O_MAX_MERGE_ACTIVE; ++i)
+        if (s->ma_block_id[i] == block_id) { a = i; break; }
+    int32_t is_new = 0;
+    if (a == -1) {
+        for (int i = 0; i < O_MAX_MERGE_ACTIVE; ++i)
+            if (s->ma_block_id[i] == -1) { a = i; break; }
+        if (a == -1) { a = 0; clear_active(s, 0); }
+        clear_active(s, a);
+        s->ma_block_id[a] = block_id;
+        is_new = 1;
+    }
+    if (s->ma_seen[a][local_idx] != 0) return;   /* duplicate -> SKIP (:177-182) */
+    s->ma_seen[a][local_idx] = 1;
+    s->ma_complete[a] = (int8_t)(s->ma_complete[a] + 1);
+
+    int32_t fin = -1;
+    if (s->ma_complete[a] >= s->block_frames) {
+        int32_t start_t = block_id * s->block_frames;
+        int32_t end_t = start_t + s->block_frames - 1;
+        int32_t median_t = (start_t + end_t) / 2;
+        int32_t ci;
+        if (s->mc_count < s->capacity) {
+            ci = s->mc_count;
+            s->mc_count = (int8_t)(s->mc_count + 1);
+        } else {
+            for (int i = 1; i < s->capacity; ++i) {
+                s->mc_slot[i - 1] = s->mc_slot[i];
+                s->mc_block_id[i - 1] = s->mc_block_id[i];
+                s->mc_start_t[i - 1] = s->mc_start_t[i];
+                s->mc_end_t[i - 1] = s->mc_end_t[i];
+                s->mc_median_t[i - 1] = s->mc_median_t[i];
+            }
+            ci = s->capacity - 1;
+        }
+        s->mc_slot[ci] = ci;
+        s->mc_block_id[ci] = block_id;
+        s->mc_start_t[ci] = start_t;
+        s->mc_end_t[ci] = end_t;
+        s->mc_median_t[ci] = median_t;
+        clear_active(s, a);
+        fin = ci;
+    }
+    d->kind = O_DST_MERGE_ACCUM;
+    d->slot = -1;
+    d->accum_slot = a;
+    d->local_idx = local_idx;
+    d->finalize_idx = fin;
+    d->is_new = is_new;
+}
+
+/* desc arrays: [H*F] each, head-major.  order: dst_kind, dst_slot, src_frame,
+ * src_head, merge_accum_slot, merge_local_idx, merge_finalize_idx,
+ * merge_is_new_block (anchor_store_update.cu:233-313). */
+void orc_state_update(uint8_t *states_bytes, const int64_t *t_vals, int H, int F,
+                      int pass_kind, int32_t *dk, int32_t *ds, int32_t *dsf,
+                      int32_t *dsh, int32_t *dma, int32_t *dml, int32_t *dmf,
+                      int32_t *dmn) {
+    OrcState *states = (OrcState *)states_bytes;
+    for (int h = 0; h < H; ++h) {
+        OrcState *s = &states[h];
+        for (int f = 0; f < F; ++f) {
+            int i = h * F + f;
+            OrcDesc d = {O_DST_SKIP, -1, -1, -1, -1, 0};
+            if (pass_kind == 1) {
+                int32_t t = (int32_t)t_vals[f];
+                switch (s->kind) {
+                case O_SK_CYCLIC: st_cyclic(s, t, &d); break;
+                case O_SK_STRIDE: st_tkeyed(s, t, &d, 1); break;
+                case O_SK_LAG: st_tkeyed(s, t, &d, 0); break;
+                case O_SK_MERGE: st_merge(s, t, &d); break;
+                default: break;
+                }
+            }
+            dk[i] = d.kind; ds[i] = d.slot; dsf[i] = f; dsh[i] = h;
+            dma[i] = d.accum_slot; dml[i] = d.local_idx;
+            dmf[i] = d.finalize_idx; dmn[i] = d.is_new;
+        }
+    }
+}
+
+/* ======================================================================== */
+/* Planner: mega_plan.cc                                                     */
+/* ======================================================================== */
+int64_t orc_map_sink_time(int64_t t, int mode, int cmin, int cmax, int lag) {
+    /* mega_plan.cc:63-80 */
+    if (mode == 1) {
+        int64_t delta = t;
+        if (delta < cmin) delta = cmin;
+        if (delta > cmax) delta = cmax;
+        int64_t out = t - delta;
+        return out < 0 ? 0 : out;
+    }
+    int64_t out = t - lag;
+    return out < 0 ? 0 : out;
+}
+
+/*
+ * Multi-chunk plan (mega_plan.cc:510-654 with emit_chunk_plan :133-264).
+ * vc: valid_count [L,H,3] int64; mtc: merge_token_count [L,H,MMB] int32;
+ * states_layer: this layer's H PerHeadStates.  Output arrays are sized
+ * [C*H*S] (S = max_sink+max_middle+max_recent+MMB) and [C*H+1] for cu;
+ * they are filled with the reference's padding values first.
+ * Returns the total packed tokens (the value compared against the pack
+ * workspace capacity at mega_plan.cc:622-629).
+ */
+int64_t orc_plan_multi(const int64_t *vc, const int32_t *mtc, const uint8_t *states_layer,
+                       int L, int H, int F, int max_sink, int max_middle, int max_recent,
+                       int mmb, int layer, const int64_t *cur_t, int C, int sink_mode,
+                       int cmin, int cmax, int lag, int32_t *cu, int32_t *sk, int32_t *sg,
+                       int32_t *sl, int32_t *dst, int64_t *traw, int64_t *tremap) {
+    (void)L;
+    const OrcState *st = (const OrcState *)states_layer;
+    const int S = max_sink + max_middle + max_recent + mmb;
+    const int N = C * H * S;
+    for (int i = 0; i < N; ++i) {
+        sk[i] = -1; sg[i] = 0; sl[i] = 0; dst[i] = 0; traw[i] = -1; tremap[i] = -1;
+    }
+    for (int i = 0; i < C * H + 1; ++i) cu[i] = 0;
+    int32_t run = 0;
+    for (int c = 0; c < C; ++c) {
+        const int64_t ct = cur_t[c];
+        const int64_t sync_t = orc_map_sink_time(ct, sink_mode, cmin, cmax, lag);
+        for (int h = 0; h < H; ++h) {
+            const OrcState *s = &st[h];
+            const int base = (c * H + h) * S;
+            int fp = 0;
+            const int thr = (int)s->sink_capacity;
+            const int64_t *vch = vc + ((int64_t)layer * H + h) * 3;
+            const int nsr = (int)vch[0];
+            const int ns = (thr > 0 && thr < nsr) ? thr : nsr;
+#define EMIT(KIND, SLOTG, LEN, TR, TM)                                         \
+    do {                                                                       \
+        int _i = base + fp;                                                    \
+        sk[_i] = (KIND); sg[_i] = (SLOTG); sl[_i] = (LEN); dst[_i] = run;      \
+        traw[_i] = (TR); tremap[_i] = (TM); run += (LEN); ++fp;                \
+    } while (0)
+            for (int k = 0; k < ns && k < max_sink; ++k)
+                EMIT(0, h * max_sink + k, F, (int64_t)k, sync_t);
+            const int nr = (int)vch[2];
+            for (int k = 0; k < nr && k < max_recent; ++k)
+                EMIT(2, h * max_recent + k, F, -1, -1);
+            if (s->kind == O_SK_CYCLIC) {
+                const int period = s->period > 0 ? s->period : 1;
+                const int bcap = s->bucket_cap > 0 ? s->bucket_cap : 1;
+                const int phase = (int)(((ct % period) + period) % period);
+                const int pb = phase * O_MAX_BUCKET;
+                const int pe = pb + (bcap < O_MAX_BUCKET ? bcap : O_MAX_BUCKET);
+                for (int i = pb; i < pe; ++i) {
+                    if (s->cyclic_slot[i] < 0) continue;
+                    if (s->cyclic_t[i] < thr) continue;
+                    EMIT(1, h * max_middle + i, F, (int64_t)s->cyclic_t[i], sync_t);
+                    if (fp >= S) break;
+                }
+            } else if (s->kind == O_SK_STRIDE || s->kind == O_SK_LAG) {
+                const int tc = (int)s->tkey_count;
+                for (int i = 0; i < tc && i < O_MAX_TKEYED; ++i) {
+                    if (s->tkey_t[i] < thr) continue;
+                    EMIT(1, h * max_middle + i, F, (int64_t)s->tkey_t[i],
+                         s->kind == O_SK_STRIDE ? sync_t : -1);
+                    if (fp >= S) break;
+                }
+            }
+            if (s->kind == O_SK_MERGE) {
+                const int mcc = (int)s->mc_count;
+                for (int i = 0; i < mcc && i < O_MAX_MERGE_BLOCKS; ++i) {
+                    const int bs = s->mc_slot[i];
+                    if (bs < 0 || bs >= mmb) continue;
+                    if (s->mc_start_t[i] <= 0) continue;
+                    const int32_t tok = mtc[((int64_t)layer * H + h) * mmb + bs];
+                    if (tok <= 0) continue;
+                    if (fp >= S) break;
+                    EMIT(3, h * mmb + bs, tok, 0, (int64_t)s->mc_median_t[i]);
+                }
+            }
+#undef EMIT
+            cu[c * H + h + 1] = run;
+        }
+    }
+    return (int64_t)run;
+}
+
+/* _mega_attention.py:349-385: shift per-layer slot ids into the [L,H,...]
+ * pool layout.  kind -1 entries are left unchanged. */
+void orc_layer_offset(const int32_t *sk, int32_t *sg, int n, int layer, int H, int max_sink,
+                      int max_middle, int max_recent, int mmb) {
+    if (layer == 0) return;
+    const int32_t off[4] = {layer * H * max_sink, layer * H * max_middle,
+                            layer * H * max_recent, layer * H * mmb};
+    for (int i = 0; i < n; ++i) {
+        if (sk[i] >= 0 && sk[i] <= 3) sg[i] += off[sk[i]];
+    }
+}
+
+/* ======================================================================== */
+/* Frame scatter: pyramidkv_update.cu:21-110                                 */
+/* ======================================================================== */
+/* new_k/new_v: [Fb, H, FSEQ, D]; new_pos: [Fb, H, FSEQ, 3] or NULL.
+ * pools: [L*H*slots, FSEQ, D] per kind (0 sink, 1 middle, 2 recent). */
+void orc_update_frames(const uint16_t *new_k, const uint16_t *new_v, const int64_t *new_pos,
+                       uint16_t *sink_k, uint16_t *sink_v, uint16_t *mid_k, uint16_t *mid_v,
+                       uint16_t *rec_k, uint16_t *rec_v, int64_t *sink_pos, int64_t *mid_pos,
+                       int64_t *rec_pos, const int32_t *dkind, const int32_t *dslot,
+                       const int32_t *sframe, const int32_t *shead, int n, int H, int FSEQ,
+                       int D) {
+    const int64_t fd = (int64_t)FSEQ * D;
+    for (int op = 0; op < n; ++op) {
+        const int kind = dkind[op];
+        if (kind < 0) continue;
+        const int64_t src = ((int64_t)sframe[op] * H + shead[op]) * fd;
+        const int64_t dbase = (int64_t)dslot[op] * fd;
+        uint16_t *dk, *dv; int64_t *dp;
+        if (kind == 0) { dk = sink_k; dv = sink_v; dp = sink_pos; }
+        else if (kind == 1) { dk = mid_k; dv = mid_v; dp = mid_pos; }
+        else { dk = rec_k; dv = rec_v; dp = rec_pos; }
+        memcpy(dk + dbase, new_k + src, (size_t)fd * 2);
+        memcpy(dv + dbase, new_v + src, (size_t)fd * 2);
+        if (new_pos && dp) {
+            const int64_t ps = ((int64_t)sframe[op] * H + shead[op]) * FSEQ * 3;
+            memcpy(dp + (int64_t)dslot[op] * FSEQ * 3, new_pos + ps, (size_t)FSEQ * 3 * 8);
+        }
+    }
+}
+
+/* ======================================================================== */
+/* Merge accumulation: mega_merge_accum.cu:52-252 (one layer's slices)       */
+/* ======================================================================== */
+/* recip_mode 0: IEEE 1/x; 1: the value the reference's fast-math build
+ * produces for power-of-two divisors is identical to IEEE, so mode 0 is used
+ * for every divisor the shipped grids produce.  Kept as a parameter so a
+ * test can flag a non-power-of-two divisor. */
+void orc_merge_accum(const uint8_t *states_bytes, const uint16_t *new_k, const uint16_t *new_v,
+                     const int64_t *new_pos, const int32_t *dkind, const int32_t *dslot,
+                     const int32_t *dfin, const int32_t *dnew, float *acc_k, float *acc_v,
+                     int64_t *acc_pos, int32_t *acc_gid, float *acc_tpg, int32_t *acc_ng,
+                     uint16_t *mk, uint16_t *mv, int64_t *mpos, int32_t *mtc, int H, int F,
+                     int FSEQ, int D, int MMA, int MMB, int MTPA) {
+    const OrcState *st = (const OrcState *)states_bytes;
+    for (int h = 0; h < H; ++h) {
+        const int32_t bf = st[h].block_frames;
+        for (int f = 0; f < F; ++f) {
+            const int di = h * F + f;
+            const int32_t kind = dkind[di], a = dslot[di], isn = dnew[di], fin = dfin[di];
+            if (kind != O_DST_MERGE_ACCUM || a < 0) continue;
+            const int64_t abase = ((int64_t)h * MMA + a) * MTPA;
+            const int64_t gbase = ((int64_t)h * MMA + a) * FSEQ;
+            const int64_t pnew = ((int64_t)f * H + h) * FSEQ * 3;
+            if (isn) {
+                const int32_t ps = st[h].patch_size;
+                for (int g = 0; g < MTPA; ++g)
+                    for (int d = 0; d < D; ++d) {
+                        acc_k[(abase + g) * D + d] = 0.0f;
+                        acc_v[(abase + g) * D + d] = 0.0f;
+                    }
+                int32_t my = -1, mx = -1;
+                for (int t = 0; t < FSEQ; ++t) {
+                    int32_t y = (int32_t)new_pos[pnew + t * 3 + 1];
+                    int32_t x = (int32_t)new_pos[pnew + t * 3 + 2];
+                    if (y > my) my = y;
+                    if (x > mx) mx = x;
+                }
+                const int32_t pc = (mx >= 0 && ps > 0) ? (mx / ps + 1) : 1;
+                const int32_t pr = (my >= 0 && ps > 0) ? (my / ps + 1) : 1;
+                const int32_t ng = pr * pc;
+                const int32_t sng = ng > MTPA ? MTPA : ng;
+                acc_ng[h * MMA + a] = sng;
+                for (int g = 0; g < MTPA; ++g) acc_tpg[abase + g] = 0.0f;
+                for (int t = 0; t < FSEQ; ++t) {
+                    int32_t y = (int32_t)new_pos[pnew + t * 3 + 1];
+                    int32_t x = (int32_t)new_pos[pnew + t * 3 + 2];
+                    int32_t py = ps > 0 ? y / ps : 0, px = ps > 0 ? x / ps : 0;
+                    int32_t gid = py * pc + px;
+                    if (gid < 0 || gid >= sng) gid = 0;
+                    acc_gid[gbase + t] = gid;
+                    acc_tpg[abase + gid] += 1.0f;
+                }
+                for (int g = 0; g < sng; ++g) acc_tpg[abase + g] *= (float)bf;
+                const int64_t tv = new_pos[pnew];
+                for (int g = 0; g < sng; ++g) {
+                    acc_pos[(abase + g) * 3 + 0] = tv;
+                    acc_pos[(abase + g) * 3 + 1] = (g / pc) * ps;
+                    acc_pos[(abase + g) * 3 + 2] = (g % pc) * ps;
+                }
+            }
+            const int64_t kbase = ((int64_t)f * H + h) * FSEQ;
+            for (int t = 0; t < FSEQ; ++t) {
+                const int32_t gid = acc_gid[gbase + t];
+                for (int d = 0; d < D; ++d) {
+                    acc_k[(abase + gid) * D + d] += bf2f(new_k[(kbase + t) * D + d]);
+                    acc_v[(abase + gid) * D + d] += bf2f(new_v[(kbase + t) * D + d]);
+                }
+            }
+            if (fin >= 0) {
+                const int32_t ng = acc_ng[h * MMA + a];
+                const int64_t pbase = ((int64_t)h * MMB + fin) * MTPA;
+                for (int t = 0; t < ng; ++t) {
+                    const float div = acc_tpg[abase + t];
+                    const float inv = div > 0.0f ? 1.0f / div : 0.0f;
+                    for (int d = 0; d < D; ++d) {
+                        mk[(pbase + t) * D + d] = f2bf(acc_k[(abase + t) * D + d] * inv);
+                        mv[(pbase + t) * D + d] = f2bf(acc_v[(abase + t) * D + d] * inv);
+                    }
+                    for (int j = 0; j < 3; ++j)
+                        mpos[(pbase + t) * 3 + j] = acc_pos[(abase + t) * 3 + j];
+                }
+                mtc[h * MMB + fin] = ng;
+            }
+        }
+    }
+}
+
+/* ======================================================================== */
+/* Pack + fused RoPE: pyramidkv_pack.cu:28-185                               */
+/* ======================================================================== */
+enum { ORC_ROPE_FMA_FIRST = 0,   /* fma(a,b, -(c*d)) / fma(a,b, c*d)       */
+       ORC_ROPE_FMA_SECOND = 1,  /* fma(-c,d, a*b)   / fma(c,d, a*b)       */
+       ORC_ROPE_NO_FMA = 2 };    /* (a*b) - (c*d), each product rounded    */
+
+static inline void rot(float kr, float ki, float fr, float fi, int mode, float *o_r,
+                       float *o_i) {
+    if (mode == ORC_ROPE_FMA_FIRST) {
+        *o_r = fmaf(kr, fr, -(ki * fi));
+        *o_i = fmaf(kr, fi, ki * fr);
+    } else if (mode == ORC_ROPE_FMA_SECOND) {
+        *o_r = fmaf(-ki, fi, kr * fr);
+        *o_i = fmaf(ki, fr, kr * fi);
+    } else {
+        volatile float a = kr * fr, b = ki * fi, c = kr * fi, d = ki * fr;
+        *o_r = a - b;
+        *o_i = c + d;
+    }
+}
+
+/* pools as in orc_update_frames plus merge pools [L*H*MMB, MTPA, D].
+ * k_out/v_out: [T, D]; pos_out: [T, 3] or NULL.  Tables: [rows, cols*2] fp32
+ * or NULL (a NULL remap or all-NULL tables disables RoPE, as in the kernel). */
+void orc_pack(const uint16_t *sink_k, const uint16_t *sink_v, const uint16_t *mid_k,
+              const uint16_t *mid_v, const uint16_t *rec_k, const uint16_t *rec_v,
+              const uint16_t *mg_k, const uint16_t *mg_v, const int64_t *sink_pos,
+              const int64_t *mid_pos, const int64_t *rec_pos, const int64_t *mg_pos,
+              uint16_t *k_out, uint16_t *v_out, int64_t *pos_out, const int32_t *sk,
+              const int32_t *sg, const int32_t *sl, const int32_t *dst, int nseg,
+              const int64_t *tremap, const float *ft, int ft_rows, int ft_cols,
+              const float *fy, int fy_rows, int fy_cols, const float *fx, int fx_rows,
+              int fx_cols, int FSEQ, int MTPA, int D, int rope_mode) {
+    const int ch = D / 2;
+    for (int s = 0; s < nseg; ++s) {
+        const int kind = sk[s];
+        if (kind < 0) continue;
+        const int len = sl[s];
+        if (len <= 0) continue;
+        const int stride_tok = kind == 3 ? MTPA : FSEQ;
+        const int64_t sb = (int64_t)sg[s] * stride_tok * D;
+        const int64_t pb = (int64_t)sg[s] * stride_tok * 3;
+        const uint16_t *srck, *srcv; const int64_t *srcp;
+        if (kind == 0) { srck = sink_k; srcv = sink_v; srcp = sink_pos; }
+        else if (kind == 1) { srck = mid_k; srcv = mid_v; srcp = mid_pos; }
+        else if (kind == 2) { srck = rec_k; srcv = rec_v; srcp = rec_pos; }
+        else { srck = mg_k; srcv = mg_v; srcp = mg_pos; }
+        srck += sb; srcv += sb;
+        if (srcp) srcp += pb;
+        uint16_t *dk = k_out + (int64_t)dst[s] * D;
+        uint16_t *dv = v_out + (int64_t)dst[s] * D;
+        const int fuse = tremap && (ft || fy || fx) && srcp;
+        const int64_t tm = fuse ? tremap[s] : -1;
+        if (fuse) {
+            for (int tok = 0; tok < len; ++tok) {
+                int64_t pt = srcp[tok * 3 + 0], py = srcp[tok * 3 + 1], px = srcp[tok * 3 + 2];
+                if (tm >= 0) pt = tm;
+                for (int p = 0; p < ch; ++p) {
+                    float fr = 1.0f, fi = 0.0f;
+                    if (p < ft_cols) {
+                        int row = (int)pt;
+                        if (row < 0) row = 0;
+                        if (row >= ft_rows) row = ft_rows - 1;
+                        fr = ft[row * ft_cols * 2 + p * 2];
+                        fi = ft[row * ft_cols * 2 + p * 2 + 1];
+                    } else if (p < ft_cols + fy_cols) {
+                        int row = (int)py;
+                        if (row < 0) row = 0;
+                        if (row >= fy_rows) row = fy_rows - 1;
+                        int c = p - ft_cols;
+                        fr = fy[row * fy_cols * 2 + c * 2];
+                        fi = fy[row * fy_cols * 2 + c * 2 + 1];
+                    } else {
+                        int row = (int)px;
+                        if (row < 0) row = 0;
+                        if (row >= fx_rows) row = fx_rows - 1;
+                        int c = p - ft_cols - fy_cols;
+                        fr = fx[row * fx_cols * 2 + c * 2];
+                        fi = fx[row * fx_cols * 2 + c * 2 + 1];
+                    }
+                    const int o = tok * D + p * 2;
+                    float nr, ni;
+                    rot(bf2f(srck[o]), bf2f(srck[o + 1]), fr, fi, rope_mode, &nr, &ni);
+                    dk[o] = f2bf(nr);
+                    dk[o + 1] = f2bf(ni);
+                }
+            }
+            memcpy(dv, srcv, (size_t)len * D * 2);
+        } else {
+            memcpy(dk, srck, (size_t)len * D * 2);
+            memcpy(dv, srcv, (size_t)len * D * 2);
+        }
+        if (pos_out && srcp) memcpy(pos_out + (int64_t)dst[s] * 3, srcp, (size_t)len * 3 * 8);
+    }
+}
