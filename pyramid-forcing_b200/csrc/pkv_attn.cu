@@ -1,0 +1,624 @@
+// Ragged-cache attention: softmax(Q K^T * scale) V for every (chunk, head)
+// segment of the packed K/V workspace, non-causal.
+//
+// Reference call: flash_attn_varlen_func at pyramidkv/_mega_cache.py:550-559
+// with Q permuted to (chunk, head, token) (:529-534) and the output permuted
+// back (:562-569); cu_seqlens_q has stride rows_per_chunk, cu_seqlens_k comes
+// from the planner.  Here Q and O are read / written in the caller's
+// [1, L_q, H, D] layout directly, so both permute copies disappear.
+//
+// B200 design (head_dim 128):
+//   * one CTA per (128-row query tile, segment); CTAs are ordered so the
+//     longest segments start first (7x spread of per-head KV lengths) and the
+//     13 query tiles of one segment run side by side, sharing K/V through L2;
+//   * warp 0 issues TMA loads (Q once, K/V 128-row tiles through a 3-stage
+//     ring, 128B-swizzled so the tiles are valid UMMA operands as loaded);
+//   * warp 1 (one elected thread) issues tcgen05.mma: S = Q K^T into one of
+//     two TMEM S buffers, then O += P V with P read from TMEM;
+//   * warps 2-5 (one thread per query row = TMEM lane) run the fp32 online
+//     softmax on S pulled out of TMEM with tcgen05.ld, write P back as bf16
+//     into the S buffer, and rescale O in TMEM only when a row maximum grows by
+//     more than 2^8 (the result is exact: the final O/l uses the same stale
+//     maximum), and normalise and store O at the end;
+//   * every wait is bounded by a wall-clock limit; on expiry the kernel
+//     raises a status bit, drains its own copies, frees TMEM and returns.
+// Other head dims use a plain CUDA-core kernel.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "pkv_common.cuh"
+
+namespace pkv {
+
+constexpr int kBM = 128;          // query rows per tile (= TMEM lanes)
+constexpr int kBN = 128;          // keys per tile
+constexpr int kHD = 128;          // head dim of the tensor-core path
+constexpr int kStages = 3;        // K/V ring depth
+constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr uint32_t kHalfBytes = kBM * 64 * 2;   // [128 rows][64 bf16] = 16 KB
+constexpr uint32_t kTileBytes = 2 * kHalfBytes; // one 128x128 bf16 tile
+constexpr uint64_t kTimeoutNs = 4000000000ull;  // 4 s per wait
+constexpr float kRescaleThreshold = 8.0f;        // log2 units
+
+struct __align__(1024) AttnSmem {
+  uint8_t q[kTileBytes];
+  uint8_t k[kStages][kTileBytes];
+  uint8_t v[kStages][kTileBytes];
+  uint64_t q_full;
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done;  // one completion per O += P V
+  uint32_t tmem_base;
+  int abort;
+  int seg, mtile;
+};
+
+// ---- PTX wrappers -----------------------------------------------------------
+__device__ __forceinline__ uint32_t su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false when the CTA is aborting (limit reached here or in
+// another role).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
+                                          int32_t* status) {
+  if (mbar_try(b, parity)) return true;
+  const uint64_t t0 = now_ns();
+  while (!mbar_try(b, parity)) {
+    if (*abort) return false;
+    if (now_ns() - t0 > kTimeoutNs) {
+      *abort = 1;
+      flag(status, PKV_ST_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          su32(bar))
+      : "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem]
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// 32 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(addr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
+          addr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// UMMA shared-memory descriptor, 128-byte swizzle (SM100 version bits = 1).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3FFFu);
+  d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+// Instruction descriptor, kind::f16: bf16 A/B, fp32 D, M=128, N=128.
+__host__ __device__ constexpr uint32_t idesc_bf16(bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(b_mn_major) << 16) |
+         (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+}
+
+struct AttnArgs {
+  const int32_t* cu;
+  int n_seg, H, rows_per_chunk, m_tiles;
+  float scale_log2;
+  uint16_t* out;
+  int64_t o_row_stride, o_head_stride;
+  int32_t* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                   const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  AttnSmem& sm = *reinterpret_cast<AttnSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  volatile int* abort = &sm.abort;
+
+  if (threadIdx.x == 0) {
+    // Longest segments first: rank = #segments longer (ties by index).
+    const int order = blockIdx.x / a.m_tiles;
+    int seg = -1;
+    for (int s = 0; s < a.n_seg && seg < 0; ++s) {
+      const int ls = a.cu[s + 1] - a.cu[s];
+      int rank = 0;
+      for (int o = 0; o < a.n_seg; ++o) {
+        const int lo = a.cu[o + 1] - a.cu[o];
+        rank += (lo > ls) || (lo == ls && o < s);
+      }
+      if (rank == order) seg = s;
+    }
+    sm.seg = seg;
+    sm.mtile = blockIdx.x - order * a.m_tiles;
+    sm.abort = 0;
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.s_full[b], 1);
+      mbar_init(&sm.p_full[b], 4);
+    }
+    mbar_init(&sm.o_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(&sm.tmem_base)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const int seg = sm.seg;
+  const int mt = sm.mtile;
+  const uint32_t tmem = sm.tmem_base;
+  const int c = seg >= 0 ? seg / a.H : 0;
+  const int h = seg >= 0 ? seg - c * a.H : 0;
+  const int kv0 = seg >= 0 ? a.cu[seg] : 0;
+  const int lk = seg >= 0 ? a.cu[seg + 1] - kv0 : 0;
+  const int nkv = (lk + kBN - 1) / kBN;
+  const int row0 = c * a.rows_per_chunk + mt * kBM;  // global query row of tile row 0
+
+  if (seg >= 0 && nkv > 0) {
+    if (warp == 0) {
+      // ---------------- TMA producer ----------------
+      if (lane == 0) {
+        mbar_expect_tx(&sm.q_full, kTileBytes);
+        tma_load_3d(sm.q, &tm_q, &sm.q_full, 0, h, row0);
+        tma_load_3d(sm.q + kHalfBytes, &tm_q, &sm.q_full, 64, h, row0);
+        int issued = 0;
+        for (int j = 0; j < nkv; ++j) {
+          const int s = j % kStages;
+          if (j >= kStages &&
+              !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, a.status))
+            break;
+          mbar_expect_tx(&sm.kv_full[s], 2 * kTileBytes);
+          const int y = kv0 + j * kBN;
+          tma_load_2d(sm.k[s], &tm_k, &sm.kv_full[s], 0, y);
+          tma_load_2d(sm.k[s] + kHalfBytes, &tm_k, &sm.kv_full[s], 64, y);
+          tma_load_2d(sm.v[s], &tm_v, &sm.kv_full[s], 0, y);
+          tma_load_2d(sm.v[s] + kHalfBytes, &tm_v, &sm.kv_full[s], 64, y);
+          issued = j + 1;
+        }
+        if (*abort) {
+          // drain this CTA's own copies before the shared memory goes away
+          mbar_wait(&sm.q_full, 0, abort, a.status);
+          for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
+            const uint64_t t0 = now_ns();
+            while (!mbar_try(&sm.kv_full[j % kStages], (j / kStages) & 1) &&
+                   now_ns() - t0 < kTimeoutNs) {
+            }
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      if (lane == 0) {
+        constexpr uint32_t id_qk = idesc_bf16(false);
+        constexpr uint32_t id_pv = idesc_bf16(true);
+        const uint32_t s_tm[2] = {tmem, tmem + 128};
+        const uint32_t o_tm = tmem + 256;
+        const uint32_t q_s = su32(sm.q);
+        bool ok = mbar_wait(&sm.q_full, 0, abort, a.status);
+        auto issue_qk = [&](int j) {
+          const int s = j % kStages;
+          const uint32_t k_s = su32(sm.k[s]);
+#pragma unroll
+          for (int kk = 0; kk < kHD / 16; ++kk) {
+            const uint32_t half = (kk >> 2) * kHalfBytes, off = (kk & 3) * 32;
+            mma_ss(s_tm[j & 1], sdesc_sw128(q_s + half + off, 16, 1024),
+                   sdesc_sw128(k_s + half + off, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&sm.s_full[j & 1]);
+        };
+        if (ok) ok = mbar_wait(&sm.kv_full[0], 0, abort, a.status);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(0);
+        }
+        for (int j = 0; ok && j < nkv; ++j) {
+          if (j + 1 < nkv) {
+            const int s1 = (j + 1) % kStages;
+            if (!mbar_wait(&sm.kv_full[s1], ((j + 1) / kStages) & 1, abort, a.status)) break;
+            tc_fence_after();
+            issue_qk(j + 1);
+          }
+          if (!mbar_wait(&sm.p_full[j & 1], (j >> 1) & 1, abort, a.status)) break;
+          tc_fence_after();
+          const uint32_t v_s = su32(sm.v[j % kStages]);
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            // A = P (TMEM, 2 bf16 per column), B = V rows kk*16.. (MN-major)
+            mma_ts(o_tm, s_tm[j & 1] + kk * 8, sdesc_sw128(v_s + kk * 2048, kHalfBytes, 1024),
+                   id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&sm.kv_empty[j % kStages]);
+          tc_commit(&sm.o_done);
+        }
+      }
+    } else {
+      // ---------------- softmax / correction / epilogue ----------------
+      const int quad = warp & 3;
+      const int row = quad * 32 + lane;
+      const uint32_t lane_off = uint32_t(quad * 32) << 16;
+      const uint32_t o_tm = tmem + 256 + lane_off;
+      float m_ref = -INFINITY;  // running reference maximum (log2 domain)
+      float l_sum = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < nkv; ++j) {
+        const uint32_t s_tm = tmem + (j & 1) * 128 + lane_off;
+        if (!mbar_wait(&sm.s_full[j & 1], (j >> 1) & 1, abort, a.status)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld32(s_tm + q * 32, sr[q]);
+        tmem_wait_ld();
+        const int valid = lk - j * kBN;  // keys of this tile inside the segment
+        float mx = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float x = (q * 32 + e < valid) ? __uint_as_float(sr[q][e]) * a.scale_log2
+                                                 : -INFINITY;
+            sr[q][e] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+        const float m_new = fmaxf(m_ref, mx);
+        const bool grow = m_new > m_ref + kRescaleThreshold || j == 0;
+        float alpha = 1.0f;
+        if (grow) {
+          alpha = (j == 0) ? 0.0f : fast_exp2(m_ref - m_new);
+          m_ref = m_new;
+        }
+        float rs = 0.0f;
+        uint32_t pr[2][32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = fast_exp2(__uint_as_float(sr[q][e]) - m_ref);
+            const float p1 = fast_exp2(__uint_as_float(sr[q][e + 1]) - m_ref);
+            rs += p0 + p1;
+            pr[q >> 1][(q & 1) * 16 + (e >> 1)] = pack_bf16x2(p0, p1);
+          }
+        l_sum = l_sum * alpha + rs;
+        tmem_st32(s_tm, pr[0]);
+        tmem_st32(s_tm + 32, pr[1]);
+        // O += P_{j-1} V_{j-1} must be complete before P_j is released (and
+        // before O is rescaled).  Waiting for every completion in order keeps
+        // the parity of this barrier exact.
+        if (j > 0) {
+          if (!mbar_wait(&sm.o_done, (j - 1) & 1, abort, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        // O *= alpha for the rows whose reference maximum moved (warp-wide op)
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t orr[32];
+            tmem_ld32(o_tm + q * 32, orr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+            tmem_st32(o_tm + q * 32, orr);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[j & 1]);
+      }
+      if (ok && mbar_wait(&sm.o_done, (nkv - 1) & 1, abort, a.status)) {
+        tc_fence_after();
+        const int grow_row = mt * kBM + row;
+        const bool store = grow_row < a.rows_per_chunk;
+        const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
+        uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + grow_row) * a.o_row_stride +
+                        int64_t(h) * a.o_head_stride;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t orr[32];
+          tmem_ld32(o_tm + q * 32, orr);
+          tmem_wait_ld();
+          if (store) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(orr[e + 0]) * inv, __uint_as_float(orr[e + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(orr[e + 2]) * inv, __uint_as_float(orr[e + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(orr[e + 4]) * inv, __uint_as_float(orr[e + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(orr[e + 6]) * inv, __uint_as_float(orr[e + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + q * 32 + e) = w;
+            }
+          }
+        }
+      }
+    }
+  } else if (seg >= 0 && warp >= 2) {
+    // empty segment: zero output rows
+    const int row = (warp & 3) * 32 + lane;
+    const int grow_row = mt * kBM + row;
+    if (grow_row < a.rows_per_chunk) {
+      uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + grow_row) * a.o_row_stride +
+                      int64_t(h) * a.o_head_stride;
+      for (int e = 0; e < kHD; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core path (any even head_dim <= 256): one thread per query row,
+// K/V tiles staged in shared memory, fp32 online softmax.
+// ---------------------------------------------------------------------------
+constexpr int kSimtRows = 64;
+constexpr int kSimtKeys = 16;
+constexpr int kSimtMaxD = 256;
+
+__global__ void __launch_bounds__(kSimtRows)
+    attn_simt_kernel(const uint16_t* __restrict__ q, int64_t q_rs, int64_t q_hs,
+                     const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                     const int32_t* __restrict__ cu, int H, int rows_per_chunk, int D,
+                     float scale, uint16_t* __restrict__ out, int64_t o_rs, int64_t o_hs) {
+  __shared__ float ks[kSimtKeys][kSimtMaxD + 1];
+  __shared__ float vs[kSimtKeys][kSimtMaxD + 1];
+  const int seg = blockIdx.y;
+  const int c = seg / H, h = seg - c * H;
+  const int r = blockIdx.x * kSimtRows + threadIdx.x;
+  const bool live = r < rows_per_chunk;
+  const int kv0 = cu[seg], lk = cu[seg + 1] - kv0;
+  float qv[kSimtMaxD], acc[kSimtMaxD];
+  const uint16_t* qr = q + int64_t(c * rows_per_chunk + (live ? r : 0)) * q_rs + int64_t(h) * q_hs;
+  for (int d = 0; d < D; ++d) {
+    qv[d] = live ? bf16_bits_to_f32(qr[d]) * scale : 0.0f;
+    acc[d] = 0.0f;
+  }
+  float m = -INFINITY, l = 0.0f;
+  for (int t0 = 0; t0 < lk; t0 += kSimtKeys) {
+    const int nt = min(kSimtKeys, lk - t0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * D; i += blockDim.x) {
+      const int t = i / D, d = i - t * D;
+      ks[t][d] = bf16_bits_to_f32(k[int64_t(kv0 + t0 + t) * D + d]);
+      vs[t][d] = bf16_bits_to_f32(v[int64_t(kv0 + t0 + t) * D + d]);
+    }
+    __syncthreads();
+    for (int t = 0; t < nt; ++t) {
+      float s = 0.0f;
+      for (int d = 0; d < D; ++d) s = fmaf(qv[d], ks[t][d], s);
+      const float mn = fmaxf(m, s);
+      const float corr = __expf(m - mn);
+      const float p = __expf(s - mn);
+      l = l * corr + p;
+      for (int d = 0; d < D; ++d) acc[d] = fmaf(p, vs[t][d], acc[d] * corr);
+      m = mn;
+    }
+  }
+  if (!live) return;
+  const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+  uint16_t* orow = out + int64_t(c * rows_per_chunk + r) * o_rs + int64_t(h) * o_hs;
+  for (int d = 0; d < D; ++d) orow[d] = static_cast<uint16_t>(f32_to_bf16_bits(acc[d] * inv));
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+static bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+                     const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
+                        strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int launch_attention(const uint16_t* q, int64_t q_rs, int64_t q_hs, const uint16_t* k,
+                     const uint16_t* v, int64_t kv_rows, const int32_t* cu, int num_chunks,
+                     int H, int rows_per_chunk, int D, float scale, uint16_t* out, int64_t o_rs,
+                     int64_t o_hs, int32_t* status, cudaStream_t stream) {
+  if (num_chunks == 0 || H == 0 || rows_per_chunk == 0) return PKV_OK;
+  if (!q || !k || !v || !cu || !out || num_chunks < 0 || H < 0 || rows_per_chunk < 0 || D <= 0)
+    return PKV_EINVAL;
+  const int n_seg = num_chunks * H;
+  const bool tc_ok = D == kHD && kv_rows > 0 && kv_rows < (int64_t(1) << 31) &&
+                     (reinterpret_cast<uintptr_t>(q) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(k) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(v) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(out) % 16 == 0) && q_rs % 8 == 0 &&
+                     q_hs % 8 == 0 && o_rs % 8 == 0 && o_hs % 8 == 0 && q_rs > 0 && q_hs >= 0 &&
+                     int64_t(num_chunks) * rows_per_chunk < (int64_t(1) << 31);
+  if (tc_ok) {
+    CUtensorMap mq, mk, mv;
+    const cuuint64_t kv_dims[2] = {cuuint64_t(kHD), cuuint64_t(kv_rows)};
+    const cuuint64_t kv_str[1] = {cuuint64_t(kHD) * 2};
+    const cuuint32_t kv_box[2] = {64, kBN};
+    const cuuint64_t q_dims[3] = {cuuint64_t(kHD), cuuint64_t(H),
+                                  cuuint64_t(num_chunks) * rows_per_chunk};
+    const cuuint64_t q_str[2] = {cuuint64_t(q_hs > 0 ? q_hs : kHD) * 2, cuuint64_t(q_rs) * 2};
+    const cuuint32_t q_box[3] = {64, 1, kBM};
+    if (make_map(&mk, k, 2, kv_dims, kv_str, kv_box) &&
+        make_map(&mv, v, 2, kv_dims, kv_str, kv_box) &&
+        make_map(&mq, q, 3, q_dims, q_str, q_box)) {
+      AttnArgs a{};
+      a.cu = cu;
+      a.n_seg = n_seg;
+      a.H = H;
+      a.rows_per_chunk = rows_per_chunk;
+      a.m_tiles = (rows_per_chunk + kBM - 1) / kBM;
+      a.scale_log2 = scale * 1.4426950408889634f;
+      a.out = out;
+      a.o_row_stride = o_rs;
+      a.o_head_stride = o_hs;
+      a.status = status;
+      const size_t smem = sizeof(AttnSmem) + 1024;
+      static bool attr_set = false;
+      if (!attr_set) {
+        if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(smem)) != cudaSuccess)
+          return PKV_ELAUNCH;
+        attr_set = true;
+      }
+      attn_tc_kernel<<<n_seg * a.m_tiles, kThreads, smem, stream>>>(mq, mk, mv, a);
+      return launch_status();
+    }
+  }
+  if (D > kSimtMaxD || (D & 1)) return PKV_EUNSUPPORTED;
+  dim3 grid((rows_per_chunk + kSimtRows - 1) / kSimtRows, n_seg);
+  attn_simt_kernel<<<grid, kSimtRows, 0, stream>>>(q, q_rs, q_hs, k, v, cu, H, rows_per_chunk,
+                                                   D, scale, out, o_rs, o_hs);
+  return launch_status();
+}
+
+}  // namespace pkv
+
+using namespace pkv;
+
+extern "C" int pkv_attention(const uint16_t* q, int64_t q_row_stride, int64_t q_head_stride,
+                             const uint16_t* k, const uint16_t* v, int64_t kv_rows,
+                             const int32_t* cu_seqlens_k, int num_chunks, int num_heads,
+                             int rows_per_chunk, int head_dim, float softmax_scale, uint16_t* out,
+                             int64_t o_row_stride, int64_t o_head_stride, pkv_stream_t stream) {
+  return launch_attention(q, q_row_stride, q_head_stride, k, v, kv_rows, cu_seqlens_k,
+                          num_chunks, num_heads, rows_per_chunk, head_dim, softmax_scale, out,
+                          o_row_stride, o_head_stride, nullptr, static_cast<cudaStream_t>(stream));
+}

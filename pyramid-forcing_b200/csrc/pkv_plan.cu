@@ -1,0 +1,258 @@
+// Device planner: the ragged K/V layout of one layer's attention call.
+//
+// Reference behaviour: pyramidkv/csrc/mega_plan.cc:133-264 (emit_chunk_plan),
+// :510-654 (mega_plan_multi) and :63-80 (map_sink_time).  For every query
+// chunk c and head h the planner lists the frames (segments) the head's
+// queries attend, in this order:
+//   sink slots     s < min(valid sink, sink_capacity)   t_remap = sync_t
+//   recent slots   r < valid recent                     t_remap = -1 (stored t)
+//   cyclic slots   of phase current_t % period, skipping t < sink_capacity,
+//                  t_remap = sync_t
+//   stride / lag   tkey slots in ring-slot order, skipping t < sink_capacity,
+//                  t_remap = sync_t (stride) / -1 (lag)
+//   merge anchors  finalized blocks with start_t > 0 and a token count,
+//                  length = token count, t_remap = median t
+// with sync_t = map_sink_time(current_t) and a running token offset; the
+// reference's quirks (recent dedup disabled, merge slot aliasing after FIFO
+// eviction, block 0 never emitted) are kept because the packed layout must be
+// bit-identical.
+//
+// B200 design: the reference pulls valid_count, merge_token_count and the
+// states to the host (3 blocking D2H copies) and pushes 7 descriptor arrays
+// back (7 H2D copies) on every call, which also blocks CUDA-graph capture.
+// Here one CTA does the whole plan in device memory: thread (c, h) walks its
+// segments once to count tokens, a block-wide exclusive scan (warp shuffles)
+// turns the counts into cu_seqlens_k, and a second walk writes the
+// descriptors at their offsets.  The capacity check becomes a status bit the
+// pack kernel also honours, so an overflowing plan never writes out of bounds.
+#include "pkv_common.cuh"
+
+namespace pkv {
+
+struct PlanArgs {
+  const int64_t* vc;        // [L,H,3]
+  const int32_t* mtc;       // [L,H,MMB]
+  const HeadState* states;  // this layer's H records
+  int layer, H, F, max_sink, max_middle, max_recent, mmb, S, C;
+  int sink_mode, cmin, cmax, lag;
+  int add_layer_offset, check_capacity;
+  int64_t capacity;
+  int64_t t[PKV_MAX_CHUNKS];
+  int32_t *cu, *sk, *sg, *sl, *dst;
+  int64_t *traw, *tremap;
+  int64_t *total_out, *counter;
+  int32_t* status;
+};
+
+__device__ __forceinline__ int64_t map_sink_time(int64_t t, int mode, int cmin, int cmax,
+                                                 int lag) {
+  if (mode == 1) {
+    int64_t delta = t;
+    if (delta < cmin) delta = cmin;
+    if (delta > cmax) delta = cmax;
+    const int64_t out = t - delta;
+    return out < 0 ? 0 : out;
+  }
+  const int64_t out = t - lag;
+  return out < 0 ? 0 : out;
+}
+
+// Calls emit(kind, slot_in_layer, len, t_raw, t_remap) for every segment of
+// (chunk c, head h) in the reference's order; returns the segment count.
+template <class Emit>
+__device__ int walk_segments(const PlanArgs& a, int c, int h, Emit&& emit) {
+  const HeadState& s = a.states[h];
+  const int64_t ct = a.t[c];
+  const int64_t sync_t = map_sink_time(ct, a.sink_mode, a.cmin, a.cmax, a.lag);
+  const int thr = s.sink_capacity;
+  const int64_t* vch = a.vc + (int64_t(a.layer) * a.H + h) * 3;
+  int fp = 0;
+  const int nsr = static_cast<int>(vch[0]);
+  const int ns = (thr > 0 && thr < nsr) ? thr : nsr;
+  for (int k = 0; k < ns && k < a.max_sink; ++k, ++fp)
+    emit(fp, kDstSink, h * a.max_sink + k, a.F, int64_t(k), sync_t);
+  const int nr = static_cast<int>(vch[2]);
+  for (int k = 0; k < nr && k < a.max_recent; ++k, ++fp)
+    emit(fp, kDstRecent, h * a.max_recent + k, a.F, int64_t(-1), int64_t(-1));
+  if (s.kind == kCyclic) {
+    const int period = s.period > 0 ? s.period : 1;
+    const int bcap = s.bucket_cap > 0 ? s.bucket_cap : 1;
+    const int phase = static_cast<int>(((ct % period) + period) % period);
+    const int pb = phase * kMaxBucket;
+    const int pe = pb + (bcap < kMaxBucket ? bcap : kMaxBucket);
+    for (int i = pb; i < pe && i < kMaxPhase * kMaxBucket; ++i) {
+      if (s.cyclic_slot[i] < 0) continue;
+      if (s.cyclic_t[i] < thr) continue;
+      emit(fp, kDstMiddle, h * a.max_middle + i, a.F, int64_t(s.cyclic_t[i]), sync_t);
+      ++fp;
+      if (fp >= a.S) break;
+    }
+  } else if (s.kind == kStride || s.kind == kLag) {
+    const int tc = s.tkey_count;
+    for (int i = 0; i < tc && i < kMaxTKeyed; ++i) {
+      if (s.tkey_t[i] < thr) continue;
+      emit(fp, kDstMiddle, h * a.max_middle + i, a.F, int64_t(s.tkey_t[i]),
+           s.kind == kStride ? sync_t : int64_t(-1));
+      ++fp;
+      if (fp >= a.S) break;
+    }
+  }
+  if (s.kind == kMerge) {
+    const int mcc = s.done_count;
+    for (int i = 0; i < mcc && i < kMaxMergeBlocks; ++i) {
+      const int bs = s.done_slot[i];
+      if (bs < 0 || bs >= a.mmb) continue;
+      if (s.done_start_t[i] <= 0) continue;
+      const int32_t tok = a.mtc[(int64_t(a.layer) * a.H + h) * a.mmb + bs];
+      if (tok <= 0) continue;
+      if (fp >= a.S) break;
+      emit(fp, kSrcMerge, h * a.mmb + bs, tok, int64_t(0), int64_t(s.done_median_t[i]));
+      ++fp;
+    }
+  }
+  return fp;
+}
+
+__global__ void plan_kernel(PlanArgs a) {
+  __shared__ int64_t warp_sums[32];
+  const int i = threadIdx.x;  // = c*H + h
+  const int n = a.C * a.H;
+  const bool active = i < n;
+  const int c = active ? i / a.H : 0;
+  const int h = active ? i - c * a.H : 0;
+
+  // pass 1: token count of (c, h)
+  int64_t mine = 0;
+  if (active) {
+    walk_segments(a, c, h, [&](int, int, int, int len, int64_t, int64_t) { mine += len; });
+  }
+  // block-wide inclusive scan of the counts (c-major, h-minor = reference order)
+  const int lane = i & 31, warp = i >> 5;
+  int64_t x = mine;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) / 32;
+    int64_t w = lane < nw ? warp_sums[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) warp_sums[lane] = w;  // inclusive per-warp prefix
+  }
+  __syncthreads();
+  const int64_t incl = x + (warp > 0 ? warp_sums[warp - 1] : 0);
+  const int64_t excl = incl - mine;
+  const int64_t total = warp_sums[(blockDim.x + 31) / 32 - 1];
+
+  if (i == 0) {
+    a.cu[0] = 0;
+    if (a.total_out) *a.total_out = total;
+    if (a.counter) atomicAdd(reinterpret_cast<unsigned long long*>(a.counter),
+                             static_cast<unsigned long long>(total));
+    if (a.check_capacity && total > a.capacity) flag(a.status, PKV_ST_PACK_OVERFLOW);
+  }
+  if (!active) return;
+  a.cu[i + 1] = static_cast<int32_t>(incl);
+
+  // pass 2: descriptors at their offsets, padding for the unused positions
+  const int base = i * a.S;
+  int64_t run = excl;
+  const int slots_of[4] = {a.max_sink, a.max_middle, a.max_recent, a.mmb};
+  const int used = walk_segments(
+      a, c, h, [&](int fp, int kind, int slot, int len, int64_t traw, int64_t tremap) {
+        const int j = base + fp;
+        int32_t sg = slot;
+        if (a.add_layer_offset) {
+          const int ki = kind == kDstSink ? 0 : kind == kDstMiddle ? 1 : kind == kDstRecent ? 2 : 3;
+          sg += a.layer * a.H * slots_of[ki];
+        }
+        a.sk[j] = kind;
+        a.sg[j] = sg;
+        a.sl[j] = len;
+        a.dst[j] = static_cast<int32_t>(run);
+        a.traw[j] = traw;
+        a.tremap[j] = tremap;
+        run += len;
+      });
+  for (int fp = used; fp < a.S; ++fp) {
+    const int j = base + fp;
+    a.sk[j] = -1;
+    a.sg[j] = 0;
+    a.sl[j] = 0;
+    a.dst[j] = 0;
+    a.traw[j] = -1;
+    a.tremap[j] = -1;
+  }
+}
+
+int launch_plan(const pkv_cache_t* c, const uint8_t* states_layer, int layer,
+                const int64_t* current_t, int num_chunks, int sink_mode, int cmin, int cmax,
+                int lag, int check_capacity, int add_layer_offset, int32_t* cu, int32_t* sk,
+                int32_t* sg, int32_t* sl, int32_t* dst, int64_t* traw, int64_t* tremap,
+                int64_t* total, int64_t* counter, cudaStream_t stream) {
+  if (!c || !states_layer || !current_t || !cu || !sk || !sg || !sl || !dst || !traw ||
+      !tremap || !c->valid_count || !c->merge_token_count)
+    return PKV_EINVAL;
+  if (num_chunks <= 0 || num_chunks > PKV_MAX_CHUNKS) return PKV_ECAPACITY;
+  if (layer < 0 || layer >= c->num_layers) return PKV_EINVAL;
+  const int n = num_chunks * c->num_heads;
+  if (n > 1024) return PKV_ECAPACITY;
+  PlanArgs a{};
+  a.vc = c->valid_count;
+  a.mtc = c->merge_token_count;
+  a.states = reinterpret_cast<const HeadState*>(states_layer);
+  a.layer = layer;
+  a.H = c->num_heads;
+  a.F = c->frame_seqlen;
+  a.max_sink = c->max_sink;
+  a.max_middle = c->max_middle;
+  a.max_recent = c->max_recent;
+  a.mmb = c->max_merge_blocks;
+  a.S = int(plan_segments_per_head(c));
+  a.C = num_chunks;
+  a.sink_mode = sink_mode;
+  a.cmin = cmin;
+  a.cmax = cmax;
+  a.lag = lag;
+  a.add_layer_offset = add_layer_offset;
+  a.check_capacity = check_capacity;
+  a.capacity = c->max_pack_tokens;
+  for (int i = 0; i < num_chunks; ++i) a.t[i] = current_t[i];
+  a.cu = cu;
+  a.sk = sk;
+  a.sg = sg;
+  a.sl = sl;
+  a.dst = dst;
+  a.traw = traw;
+  a.tremap = tremap;
+  a.total_out = total;
+  a.counter = counter;
+  a.status = c->status;
+  const int threads = ((n + 31) / 32) * 32;
+  plan_kernel<<<1, threads, 0, stream>>>(a);
+  return launch_status();
+}
+
+}  // namespace pkv
+
+using namespace pkv;
+
+extern "C" int pkv_plan(const pkv_cache_t* c, const uint8_t* states_layer, int layer_idx,
+                        const int64_t* current_t, int num_chunks, int sink_mode_code,
+                        int sink_clamp_min, int sink_clamp_max, int decoupled_sink_lag,
+                        int check_capacity, int add_layer_offset, int32_t* cu_seqlens_k,
+                        int32_t* src_kind, int32_t* src_slot_global, int32_t* seg_lengths,
+                        int32_t* dst_token_offsets, int64_t* anchor_t_raw,
+                        int64_t* anchor_t_remap, int64_t* total_tokens, int64_t* token_counter,
+                        pkv_stream_t stream) {
+  return launch_plan(c, states_layer, layer_idx, current_t, num_chunks, sink_mode_code,
+                     sink_clamp_min, sink_clamp_max, decoupled_sink_lag, check_capacity,
+                     add_layer_offset, cu_seqlens_k, src_kind, src_slot_global, seg_lengths,
+                     dst_token_offsets, anchor_t_raw, anchor_t_remap, total_tokens,
+                     token_counter, static_cast<cudaStream_t>(stream));
+}

@@ -177,7 +177,7 @@ def gen_compositions(factory, mega_cache, ops, rng):
     with tempfile.TemporaryDirectory() as td:
         csv = os.path.join(td, "labels.csv")
         with open(csv, "w") as f:
-            f.write(",".join(f"h{h}" for h in range(H)) + "\n")
+            # one row per layer, no header (pyramidkv/factory.py:105-127)
             for l in range(L):
                 f.write(",".join(str(int(x)) for x in labels[l]) + "\n")
         for name, r in routings.items():
@@ -224,6 +224,21 @@ def gen_freq_tables(full):
                         ft=flat[0][rows], fy=flat[1][rows], fx=flat[2][rows])
 
 
+def gen_api(reference: str):
+    """The reference's torch library surface (op schemas, class methods), read
+    as text from pyramidkv/csrc/scatter_copy_bind.cpp:763-945."""
+    import json
+    import re
+    src = open(os.path.join(reference, "pyramidkv", "csrc", "scatter_copy_bind.cpp")).read()
+    body = src[src.index("TORCH_LIBRARY(adahead, m)"):src.index("TORCH_LIBRARY_IMPL(adahead, CUDA")]
+    methods = re.findall(r'\.def\("([A-Za-z_0-9]+)"', body)
+    schemas = []
+    for block in re.findall(r'm\.def\(\s*((?:"[^"]*"\s*)+)\)', body):
+        schemas.append("".join(re.findall(r'"([^"]*)"', block)))
+    with open(os.path.join(HERE, "adahead_api.json"), "w") as f:
+        json.dump({"class_methods": methods, "schemas": schemas}, f, indent=1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -242,6 +257,7 @@ def main():
     gen_rope(rope, full, rng)
     gen_sink_time(rope)
     gen_compositions(factory, mega_cache, ops, rng)
+    gen_api(args.reference)
     del torch
     print(f"wrote {n} state cases + rope, sink_time, compositions fixtures to {HERE}")
 
