@@ -1,0 +1,87 @@
+"""Ragged attention kernel vs a plain PyTorch fp32 reference.
+
+The reference's attention is flash_attn_varlen_func over the packed K/V
+(pyramidkv/_mega_cache.py:529-569), pinned by its own tests only against an
+fp32 softmax (tests/test_mega_readout.py:43-56).  Tolerance (bf16 output vs
+fp32 reference): max abs 2e-2, mean abs 2e-3.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+
+
+def _reference(q, k, v, cu, C, H, Lq, scale):
+    out = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+    for c in range(C):
+        for h in range(H):
+            i = c * H + h
+            a, b = int(cu[i]), int(cu[i + 1])
+            if b <= a:
+                continue
+            qh = q[c * Lq:(c + 1) * Lq, h].float()
+            s = (qh @ k[a:b].float().T) * scale
+            out[c * Lq:(c + 1) * Lq, h] = torch.softmax(s, dim=-1) @ v[a:b].float()
+    return out
+
+
+def _case(cuda, C, H, Lq, D, lens, seed=0, kv_scale=1.0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(C * Lq, H, D, generator=g).to(cuda, torch.bfloat16)
+    T = int(sum(lens))
+    k = (torch.randn(T + 7, D, generator=g) * kv_scale).to(cuda, torch.bfloat16)
+    v = torch.randn(T + 7, D, generator=g).to(cuda, torch.bfloat16)
+    cu = torch.zeros(C * H + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(torch.tensor(lens, dtype=torch.int32), 0)
+    return q, k, v, cu.to(cuda)
+
+
+def _check(out, ref):
+    err = (out.float() - ref).abs()
+    assert torch.isfinite(out.float()).all()
+    assert err.max().item() <= MAX_ABS, f"max abs err {err.max().item()}"
+    assert err.mean().item() <= MEAN_ABS, f"mean abs err {err.mean().item()}"
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_ragged_attention_matches_fp32(cuda, D):
+    from pyramidkv import _ops
+    C, H, Lq = 2, 3, 1560                     # 1560 = 12 full 128-row tiles + a 24-row tail
+    lens = [4680, 1560, 390, 9360, 4680 + 390, 777]   # frame / merge-anchor granular + ragged
+    q, k, v, cu = _case(cuda, C, H, Lq, D, lens)
+    scale = D ** -0.5
+    out = _ops.ops().pkv_attention(q, k, v, cu, C, Lq, scale)
+    _check(out, _reference(q, k, v, cu, C, H, Lq, scale))
+
+
+def test_attention_rescale_path_and_empty_segment(cuda):
+    """Large logits force the running-max rescale of O; an empty segment gives
+    zeros (flash-attn's convention for seqlen_k = 0)."""
+    from pyramidkv import _ops
+    C, H, Lq, D = 1, 3, 200, 128
+    lens = [3000, 0, 515]
+    q, k, v, cu = _case(cuda, C, H, Lq, D, lens, seed=3, kv_scale=6.0)
+    # ascending key magnitude so the row max keeps growing across tiles
+    ramp = torch.linspace(0.2, 3.0, k.shape[0], device=cuda).unsqueeze(1)
+    k = (k.float() * ramp).to(torch.bfloat16)
+    out = _ops.ops().pkv_attention(q, k, v, cu, C, Lq, 0.088)
+    ref = _reference(q, k, v, cu, C, H, Lq, 0.088)
+    _check(out, ref)
+    assert out[:, 1].abs().max().item() == 0.0
+
+
+def test_attention_strided_q_layout(cuda):
+    """Q as a non-contiguous view ([1, L_q, H, D] sliced from a wider tensor)."""
+    from pyramidkv import _ops
+    C, H, Lq, D = 3, 2, 320, 128
+    lens = [1000, 2000, 640, 128, 1, 4000]
+    q, k, v, cu = _case(cuda, C, H, Lq, D, lens, seed=7)
+    wide = torch.zeros(C * Lq, H + 2, D, device=cuda, dtype=torch.bfloat16)
+    wide[:, 1:H + 1] = q
+    qv = wide[:, 1:H + 1]
+    out = _ops.ops().pkv_attention(qv, k, v, cu, C, Lq, D ** -0.5)
+    _check(out, _reference(q, k, v, cu, C, H, Lq, D ** -0.5))

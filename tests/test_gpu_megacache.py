@@ -1,0 +1,138 @@
+"""MegaCache end to end (update + attend over many blocks) vs the oracle.
+
+The oracle restates the reference's orchestration (pyramidkv/_mega_cache.py
+:136-569) on numpy pools; the product runs the fused device ops.  After every
+call the cache state must be bit-identical: valid_count, every pool (K, V,
+pos), the committed snapshot, the state bytes, the merge anchors, and the
+packed K/V the attention read (RoPE-rotated K included).  The attention output
+is checked against the oracle's fp32 attention within the bf16 tolerance.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import pkv_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _u16(t):
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _bf16(a, dev):
+    return torch.from_numpy(a.astype(np.uint16).view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def _build(cuda, labels, routing, W, Hgrid, D=128, sink_mode="window_clamp"):
+    from pyramidkv import _mega_cache, policy
+    labels = np.asarray(labels)
+    L, H = labels.shape
+    FSEQ = W * Hgrid
+    states, caps = policy.states_from_labels(labels, routing)
+    (ft, fy, fx), full = O.rope_freq_tables(D)
+    comps = [[_Comp(policy.head_state(int(x), routing)) for x in row] for row in labels]
+    caches = _mega_cache.build_mega_caches(
+        L, H, D, FSEQ, 3, 24, 4, comps, max_attend_chunks=8, device="cuda:0",
+        sink_time_mapping_mode=sink_mode, sink_time_clamp_min=18, sink_time_clamp_max=21,
+        spatial_width=W, spatial_height=Hgrid, freqs=full)
+    orc = O.OracleMegaCache(L, H, D, FSEQ, 3, 24, 4, states, caps, spatial_width=W,
+                            sink_time_mapping_mode=sink_mode, sink_time_clamp_min=18,
+                            sink_time_clamp_max=21, freq_tables=(ft, fy, fx),
+                            rope_mode=O.ROPE_FMA_FIRST)
+    np.testing.assert_array_equal(caches[0].ctx.states_bytes.cpu().numpy(), orc.states)
+    return caches, orc
+
+
+class _Comp:
+    """Duck-typed HeadComposition carrying an already-built PerHeadState."""
+
+    def __init__(self, st):
+        self._st = st
+        self.sink_frames = st.sink_capacity
+        from pyramidkv import _mega_state_ref as ref
+        kind = st.kind
+        if kind == ref.SK_CYCLIC:
+            self.middle_strategies = [type("CyclicStrategy", (), dict(period=st.period,
+                                                                     bucket_cap=st.bucket_cap))()]
+        elif kind == ref.SK_STRIDE:
+            self.middle_strategies = [type("StrideStrategy", (), dict(interval=st.interval,
+                                                                     capacity=st.capacity))()]
+        elif kind == ref.SK_MERGE:
+            self.middle_strategies = [type("MergeStrategy", (), dict(patch_size=st.patch_size,
+                                                                    capacity=st.capacity))()]
+        else:
+            self.middle_strategies = []
+
+
+def _compare_state(cache, orc, layer, where):
+    mgr, ctx = cache.ctx.mgr, cache.ctx
+    chk = np.testing.assert_array_equal
+    chk(mgr.valid_count().cpu().numpy(), orc.vc, err_msg=f"{where}: valid_count")
+    chk(ctx.committed_vc.cpu().numpy(), orc.committed_vc, err_msg=f"{where}: committed_vc")
+    chk(ctx.states_bytes.cpu().numpy(), orc.states, err_msg=f"{where}: states")
+    for name, ok, ov, op in (("sink", orc.sink_k, orc.sink_v, orc.sink_pos),
+                             ("middle", orc.mid_k, orc.mid_v, orc.mid_pos),
+                             ("recent", orc.rec_k, orc.rec_v, orc.rec_pos)):
+        chk(_u16(getattr(mgr, f"{name}_k_pool")()).reshape(ok.shape), ok, err_msg=f"{where}: {name}_k")
+        chk(_u16(getattr(mgr, f"{name}_v_pool")()).reshape(ov.shape), ov, err_msg=f"{where}: {name}_v")
+        chk(getattr(mgr, f"{name}_pos_pool")().cpu().numpy(), op, err_msg=f"{where}: {name}_pos")
+    chk(_u16(ctx.committed_recent_k).reshape(orc.committed_rec_k.shape), orc.committed_rec_k,
+        err_msg=f"{where}: committed recent k")
+    chk(ctx.committed_recent_pos.cpu().numpy(), orc.committed_rec_pos,
+        err_msg=f"{where}: committed recent pos")
+    chk(_u16(mgr.merge_k_pool()).reshape(orc.mg_k.shape), orc.mg_k, err_msg=f"{where}: merge_k")
+    chk(mgr.merge_pos_pool().cpu().numpy(), orc.mg_pos, err_msg=f"{where}: merge_pos")
+    chk(mgr.merge_token_count().cpu().numpy(), orc.mtc, err_msg=f"{where}: merge_token_count")
+
+
+@pytest.mark.parametrize("routing,W,Hgrid", [("baseline", 13, 8), ("yaml", 52, 30)])
+def test_megacache_blocks_match_oracle(cuda, routing, W, Hgrid):
+    rng = np.random.default_rng(17)
+    labels = np.array([[-1, 1, 2, -1], [2, 2, 1, -1]])
+    caches, orc = _build(cuda, labels, routing, W, Hgrid)
+    L, H = labels.shape
+    D, FSEQ, F = 128, W * Hgrid, 3
+    n_blocks = 9 if W == 52 else 14
+    for blk in range(n_blocks):
+        start = blk * F * FSEQ
+        for mode in ("noisy", "noisy", "clean"):
+            for layer in range(L):
+                k = O.f32_to_bf16(rng.standard_normal((1, F * FSEQ, H, D)).astype(np.float32))
+                v = O.f32_to_bf16(rng.standard_normal((1, F * FSEQ, H, D)).astype(np.float32))
+                q = O.f32_to_bf16(rng.standard_normal((1, F * FSEQ, H, D)).astype(np.float32))
+                orc.update(layer, k, v, start, mode)
+                caches[layer].update(_bf16(k, cuda).view(1, -1, H, D),
+                                     _bf16(v, cuda).view(1, -1, H, D), start,
+                                     cache_update_mode=mode)
+                want, pk = orc.attend(layer, q, start)
+                got = caches[layer].attend(_bf16(q, cuda).view(1, -1, H, D), start)
+                torch.cuda.synchronize()
+                where = f"block {blk} {mode} layer {layer}"
+                _compare_state(caches[layer], orc, layer, where)
+                mgr = caches[layer].ctx.mgr
+                total = pk["total"]
+                np.testing.assert_array_equal(mgr.cu_seqlens_k()[:3 * H + 1].cpu().numpy(),
+                                              pk["cu"], err_msg=where)
+                np.testing.assert_array_equal(_u16(mgr.k_flat_out()[:total]).reshape(total, D),
+                                              pk["k"], err_msg=f"{where}: packed K")
+                np.testing.assert_array_equal(_u16(mgr.v_flat_out()[:total]).reshape(total, D),
+                                              pk["v"], err_msg=f"{where}: packed V")
+                err = (got.float().cpu().numpy() - want).__abs__()
+                assert err.max() <= 2e-2 and err.mean() <= 2e-3, (where, err.max(), err.mean())
+    assert caches[0].ctx.check_status() == 0
+    assert orc.mtc.max() > 0 or routing == "yaml"
+
+
+def test_update_rejects_bad_shapes(cuda):
+    caches, _ = _build(cuda, np.array([[1, 2]]), "baseline", 13, 8)
+    with pytest.raises((AssertionError, RuntimeError)):
+        caches[0].update(torch.zeros(1, 100, 2, 128, device=cuda, dtype=torch.bfloat16),
+                         torch.zeros(1, 100, 2, 128, device=cuda, dtype=torch.bfloat16), 0)
+    # unknown mode is a no-op, as in the reference
+    caches[0].update(torch.zeros(1, 104, 2, 128, device=cuda, dtype=torch.bfloat16),
+                     torch.zeros(1, 104, 2, 128, device=cuda, dtype=torch.bfloat16), 0,
+                     cache_update_mode="other")
+    assert int(caches[0].ctx.mgr.valid_count().abs().sum()) == 0
