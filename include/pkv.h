@@ -251,6 +251,26 @@ int pkv_attend(const pkv_cache_t *cache, const uint8_t *states_layer, int layer_
                pkv_stream_t stream);
 
 /*
+ * The two halves of pkv_attend, for callers that schedule or time them
+ * separately: pkv_attend_pack runs the planner (layer offsets applied,
+ * capacity checked, cu_seqlens_k written to cache->cu_seqlens_k) and the
+ * RoPE-fused pack into cache->k_flat / v_flat; pkv_attend_attention runs the
+ * ragged attention over what the last pkv_attend_pack on this cache wrote.
+ * Replaces: the same two stages of MegaCache.attend
+ * (pyramidkv/_mega_cache.py:466-523 and :525-569).
+ */
+int pkv_attend_pack(const pkv_cache_t *cache, const uint8_t *states_layer, int layer_idx,
+                    int num_chunks, int64_t first_t, int sink_mode_code, int sink_clamp_min,
+                    int sink_clamp_max, int decoupled_sink_lag, const float *freqs_ft,
+                    int ft_rows, int ft_cols, const float *freqs_fy, int fy_rows, int fy_cols,
+                    const float *freqs_fx, int fx_rows, int fx_cols, int64_t *token_counter,
+                    pkv_stream_t stream);
+int pkv_attend_attention(const pkv_cache_t *cache, const uint16_t *q, int64_t q_tok_stride,
+                         int64_t q_head_stride, int num_chunks, float softmax_scale,
+                         uint16_t *out, int64_t o_tok_stride, int64_t o_head_stride,
+                         pkv_stream_t stream);
+
+/*
  * Evaluation order of the RoPE pair rotation in the pack kernel: 0 =
  * fma(kr, fr, -(ki*fi)) / fma(kr, fi, ki*fr) (default), 1 = fma on the second
  * product, 2 = no contraction.  Returns the previous order.  No counterpart in

@@ -77,7 +77,7 @@ def lib():
             L.orc_map_sink_time.argtypes = [ctypes.c_int64, I, I, I, I]
             L.orc_state_update.argtypes = [P, P, I, I, I] + [P] * 8
             L.orc_plan_multi.restype = ctypes.c_int64
-            L.orc_plan_multi.argtypes = [P, P, P] + [I] * 9 + [P, I, I, I, I, I] + [P] * 7
+            L.orc_plan_multi.argtypes = [P, P, P] + [I] * 8 + [P, I, I, I, I, I] + [P] * 7
             L.orc_layer_offset.argtypes = [P, P, I, I, I, I, I, I, I]
             L.orc_update_frames.argtypes = [P] * 16 + [I] * 4
             L.orc_merge_accum.argtypes = [P] * 18 + [I] * 7

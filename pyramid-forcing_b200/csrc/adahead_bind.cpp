@@ -523,24 +523,24 @@ void op_cache_update(Mgr mgr, Tensor states_all, int64_t layer, Tensor new_k, Te
            "MegaCache.update");
 }
 
-Tensor op_attend(Mgr mgr, Tensor states_layer, int64_t layer, Tensor q, int64_t first_t,
-                  int64_t sink_mode, int64_t cmin, int64_t cmax, int64_t lag, Tensor ft,
-                  Tensor fy, Tensor fx, double scale, Tensor token_counter) {
-  require_cuda_bf16(mgr, "MegaCache.attend");
-  TORCH_CHECK(q.dim() == 4 && q.size(0) == 1, "MegaCache.attend: B>1 not yet supported");
-  TORCH_CHECK(q.size(2) == mgr->num_heads() && q.size(3) == mgr->head_dim(),
-              "MegaCache.attend: head count / head dim mismatch");
-  TORCH_CHECK(q.size(1) % mgr->frame_seqlen() == 0, "L_q (", q.size(1),
-              ") must be a multiple of FSEQ (", mgr->frame_seqlen(), ")");
-  const int64_t chunks = q.size(1) / mgr->frame_seqlen();
+int64_t attend_chunks(const Mgr& mgr, int64_t L_q) {
+  TORCH_CHECK(L_q % mgr->frame_seqlen() == 0, "L_q (", L_q, ") must be a multiple of FSEQ (",
+              mgr->frame_seqlen(), ")");
+  const int64_t chunks = L_q / mgr->frame_seqlen();
   TORCH_CHECK(chunks <= mgr->max_attend_chunks(), "mega_plan_multi: packed tokens exceed "
               "pack-workspace capacity (", mgr->max_pack_tokens(), "). Either reduce chunks (",
               chunks, ") or rebuild the manager with a larger max_attend_chunks (currently ",
               mgr->max_attend_chunks(), ").");
-  const c10::cuda::CUDAGuard g(q.device());
-  auto qq = q.scalar_type() == at::kBFloat16 ? q : q.to(at::kBFloat16);
-  if (qq.stride(3) != 1) qq = qq.contiguous();
-  auto out = at::empty({1, q.size(1), q.size(2), q.size(3)}, qq.options());
+  return chunks;
+}
+
+// Plan + RoPE-fused pack of one layer (first half of MegaCache.attend).
+void op_attend_pack(Mgr mgr, Tensor states_layer, int64_t layer, int64_t L_q, int64_t first_t,
+                    int64_t sink_mode, int64_t cmin, int64_t cmax, int64_t lag, Tensor ft,
+                    Tensor fy, Tensor fx, Tensor token_counter) {
+  require_cuda_bf16(mgr, "MegaCache.attend");
+  const int64_t chunks = attend_chunks(mgr, L_q);
+  const c10::cuda::CUDAGuard g(mgr->device());
   auto table = [](const Tensor& t, int& rows, int& cols) -> const float* {
     if (!t.defined() || t.numel() == 0) { rows = cols = 0; return nullptr; }
     TORCH_CHECK(t.dim() == 2 && t.dtype() == at::kFloat && t.is_contiguous() && t.is_cuda(),
@@ -555,12 +555,10 @@ Tensor op_attend(Mgr mgr, Tensor states_layer, int64_t layer, Tensor q, int64_t 
   const float* px = table(fx, xr, xc);
   auto c = mgr->view();
   auto sb = states_layer.contiguous();
-  check_rc(pkv_attend(&c, sb.data_ptr<uint8_t>(), int(layer),
-                      reinterpret_cast<const uint16_t*>(qq.data_ptr()), qq.stride(1),
-                      qq.stride(2), int(chunks), first_t, int(sink_mode), int(cmin), int(cmax),
-                      int(lag), pt, tr, tc, py, yr, yc, px, xr, xc, float(scale),
-                      reinterpret_cast<uint16_t*>(out.data_ptr()), out.stride(1), out.stride(2),
-                      ptr_or_null<int64_t>(token_counter), stream_of(qq)),
+  check_rc(pkv_attend_pack(&c, sb.data_ptr<uint8_t>(), int(layer), int(chunks), first_t,
+                           int(sink_mode), int(cmin), int(cmax), int(lag), pt, tr, tc, py, yr,
+                           yc, px, xr, xc, ptr_or_null<int64_t>(token_counter),
+                           stream_of(sb)),
            "MegaCache.attend");
   if (plan_bound(mgr, chunks) > mgr->max_pack_tokens() && !capturing(mgr)) {
     const int32_t st = take_status(mgr);
@@ -570,7 +568,36 @@ Tensor op_attend(Mgr mgr, Tensor states_layer, int64_t layer, Tensor q, int64_t 
                 ") or rebuild the manager with a larger max_attend_chunks (currently ",
                 mgr->max_attend_chunks(), ").");
   }
+}
+
+// Ragged attention over the last pack (second half of MegaCache.attend);
+// q and the result are [1, L_q, H, D].
+Tensor op_attend_attention(Mgr mgr, Tensor q, double scale) {
+  require_cuda_bf16(mgr, "MegaCache.attend");
+  TORCH_CHECK(q.dim() == 4 && q.size(0) == 1, "MegaCache.attend: B>1 not yet supported");
+  TORCH_CHECK(q.size(2) == mgr->num_heads() && q.size(3) == mgr->head_dim(),
+              "MegaCache.attend: head count / head dim mismatch");
+  const int64_t chunks = attend_chunks(mgr, q.size(1));
+  const c10::cuda::CUDAGuard g(q.device());
+  auto qq = q.scalar_type() == at::kBFloat16 ? q : q.to(at::kBFloat16);
+  if (qq.stride(3) != 1) qq = qq.contiguous();
+  auto out = at::empty({1, q.size(1), q.size(2), q.size(3)}, qq.options());
+  auto c = mgr->view();
+  check_rc(pkv_attend_attention(&c, reinterpret_cast<const uint16_t*>(qq.data_ptr()),
+                                qq.stride(1), qq.stride(2), int(chunks), float(scale),
+                                reinterpret_cast<uint16_t*>(out.data_ptr()), out.stride(1),
+                                out.stride(2), stream_of(qq)),
+           "MegaCache.attend");
   return out;
+}
+
+Tensor op_attend(Mgr mgr, Tensor states_layer, int64_t layer, Tensor q, int64_t first_t,
+                 int64_t sink_mode, int64_t cmin, int64_t cmax, int64_t lag, Tensor ft,
+                 Tensor fy, Tensor fx, double scale, Tensor token_counter) {
+  TORCH_CHECK(q.dim() == 4 && q.size(0) == 1, "MegaCache.attend: B>1 not yet supported");
+  op_attend_pack(mgr, states_layer, layer, q.size(1), first_t, sink_mode, cmin, cmax, lag, ft,
+                 fy, fx, token_counter);
+  return op_attend_attention(mgr, q, scale);
 }
 
 Tensor op_attention(Tensor q, Tensor k, Tensor v, Tensor cu, int64_t num_chunks,
@@ -754,6 +781,12 @@ TORCH_LIBRARY(adahead, m) {
         "int sink_clamp_min, int sink_clamp_max, int decoupled_sink_lag, Tensor freqs_ft_flat, "
         "Tensor freqs_fy_flat, Tensor freqs_fx_flat, float softmax_scale, "
         "Tensor(a!) token_counter) -> Tensor");
+  m.def("pkv_attend_pack(__torch__.torch.classes.adahead.PyramidKVCacheManager mgr, "
+        "Tensor states_layer, int layer_idx, int L_q, int first_t, int sink_mode_code, "
+        "int sink_clamp_min, int sink_clamp_max, int decoupled_sink_lag, Tensor freqs_ft_flat, "
+        "Tensor freqs_fy_flat, Tensor freqs_fx_flat, Tensor(a!) token_counter) -> ()");
+  m.def("pkv_attend_attention(__torch__.torch.classes.adahead.PyramidKVCacheManager mgr, "
+        "Tensor q, float softmax_scale) -> Tensor");
   m.def("pkv_attention(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens_k, int num_chunks, "
         "int rows_per_chunk, float softmax_scale) -> Tensor");
   m.def("pkv_status(__torch__.torch.classes.adahead.PyramidKVCacheManager mgr) -> int");
@@ -771,6 +804,8 @@ TORCH_LIBRARY_IMPL(adahead, CUDA, m) {
   m.impl("mega_merge_accum", mega_merge_accum);
   m.impl("pkv_cache_update", op_cache_update);
   m.impl("pkv_attend", op_attend);
+  m.impl("pkv_attend_pack", op_attend_pack);
+  m.impl("pkv_attend_attention", op_attend_attention);
   m.impl("pkv_attention", op_attention);
 }
 
