@@ -1,0 +1,479 @@
+#!/usr/bin/env python
+"""Benchmark: the per-layer-step KV-cache path of causal Wan2.1-T2V-1.3B.
+
+Metric: cache-update + ragged-attention microseconds per DiT
+layer-step, reported as latent frames/s.  One "step" is one 120-latent-frame
+video's cache path (configs[1], C2): 40 blocks of 3 latent frames, each block
+4 noisy + 1 clean forwards, each forward 30 layers of
+``MegaCache.update(k, v)`` + ``MegaCache.attend(q)`` -- 6000 layer-steps.
+12 heads x 128, 1560 tokens per latent frame (30 x 52), sink/middle/recent
+pools 3/24/4 frames, window_clamp(18, 21) sink time, a seeded random [30, 12]
+label matrix over {-1, 1, 2} under the BASELINE routing (stride for 1,
+periodic for 2, merge for -1).  The DiT's GEMMs, text encoder and VAE are
+outside the path and not run; Q/K/V are seeded N(0, 1) bf16 tensors from a
+rotating set of 8 (inputs + cache pools are larger than L2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs N independent videos, one per rank (weak scaling, no collective on
+the data path).  ``--impl reference`` times the CPU oracle port of the
+reference path on the host cores (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "pyramid-forcing_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "cache-update+ragged-attn µs per DiT layer-step; latent frames/sec"
+L_, H_, D_, W_, HG_ = 30, 12, 128, 52, 30
+FSEQ = W_ * HG_
+FRAMES_PER_BLOCK = 3
+PASSES = ("noisy", "noisy", "noisy", "noisy", "clean")
+N_SETS = 8
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--frames", type=int, default=120)
+    ap.add_argument("--merge-fraction", type=float, default=None,
+                    help="exact share of merge heads (configs[2] uses 0.5)")
+    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+def workload_config(args):
+    cfg = {"workload": ("C2 cache path of causal Wan2.1-T2V-1.3B: %d latent frames, 30 layers x "
+                        "12 heads x 128, 1560 tokens/frame, 3-frame blocks x (4 noisy + 1 clean)"
+                        % args.frames),
+           "layers": L_, "heads": H_, "head_dim": D_, "frame_tokens": FSEQ,
+           "frames_per_block": FRAMES_PER_BLOCK, "passes_per_block": len(PASSES),
+           "latent_frames": args.frames, "pools_frames": {"sink": 3, "middle": 24, "recent": 4},
+           "routing": "baseline (1: stride, 2: periodic, -1: merge)",
+           "labels": "seeded uniform [30,12]" if args.merge_fraction is None
+           else f"seeded, merge share {args.merge_fraction}",
+           "l2": "inputs larger than L2 (multi-GB cache pools, 8 rotating Q/K/V sets)"}
+    return cfg
+
+
+class Workload:
+    """30 MegaCache layers + rotating device inputs for one video."""
+
+    @staticmethod
+    def build(device, seed: int, merge_fraction=None):
+        import torch
+        from pyramidkv import _mega_cache, policy
+
+        w = Workload.__new__(Workload)
+        w.device = device
+        w.labels = policy.random_labels(L_, H_, seed=seed, merge_fraction=merge_fraction)
+        comps = policy.compositions_from_labels(w.labels, "baseline")
+        w.caches = _mega_cache.build_mega_caches(
+            L_, H_, D_, FSEQ, 3, 24, 4, comps, max_attend_chunks=8, device=str(device),
+            sink_time_mapping_mode="window_clamp", sink_time_clamp_min=18,
+            sink_time_clamp_max=21, spatial_width=W_, spatial_height=HG_,
+            freqs=rope_table(D_))
+        w.ctx = w.caches[0].ctx
+        w.init_states = w.ctx.states_bytes.clone()
+        w.ctx.token_counter = torch.zeros(1, dtype=torch.int64, device=device)
+        g = torch.Generator(device=device).manual_seed(1000 + seed)
+        shape = (1, FRAMES_PER_BLOCK * FSEQ, H_, D_)
+        w.sets = [tuple(torch.randn(shape, generator=g, device=device, dtype=torch.bfloat16)
+                        for _ in range(3)) for _ in range(N_SETS)]
+        return w
+
+    def reset(self):
+        """Empty cache, initial strategy states (start of a new video)."""
+        ctx = self.ctx
+        ctx.mgr.reset()
+        ctx.states_bytes.copy_(self.init_states)
+        if ctx.committed_vc is not None:
+            ctx.committed_vc.zero_()
+
+
+def rope_table(d: int):
+    """The model's RoPE table (wan/modules/causal_model.py:586-591 layout):
+    complex128 [1024, d/2] = polar(1, t * 10000^(-2i/dim)) for the t / y / x
+    parts of sizes d - 4(d//6), 2(d//6), 2(d//6)."""
+    import torch
+
+    def part(dim):
+        inv = 1.0 / torch.pow(10000, torch.arange(0, dim, 2).to(torch.float64).div(dim))
+        ang = torch.outer(torch.arange(1024), inv)
+        return torch.polar(torch.ones_like(ang), ang)
+
+    return torch.cat([part(d - 4 * (d // 6)), part(2 * (d // 6)), part(2 * (d // 6))], dim=1)
+
+
+def run_video(w, frames: int, inputs=None, hooks=None):
+    """One video's cache path.  inputs(i) -> (q, k, v) for layer-step i (default:
+    the rotating device sets); hooks: (before_update, after_update, after_attend)
+    callables receiving the layer-step index."""
+    caches = w.caches
+    i = 0
+    n_blocks = frames // FRAMES_PER_BLOCK
+    for blk in range(n_blocks):
+        start = blk * FRAMES_PER_BLOCK * FSEQ
+        for mode in PASSES:
+            for layer in range(L_):
+                q, k, v = inputs(i) if inputs is not None else w.sets[i % N_SETS]
+                if hooks:
+                    hooks[0](i)
+                caches[layer].update(k, v, start, cache_update_mode=mode)
+                if hooks:
+                    hooks[1](i)
+                out = caches[layer].attend(q, start)
+                if hooks:
+                    hooks[2](i, out)
+                i += 1
+    return i
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+_CLOCK_FIELDS = ["clocks.sm", "clocks.max.sm", "power.draw",
+                 "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+                 "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+
+def clocks_start(gpu: int):
+    path = os.path.join("/tmp", f"pkv_clocks_{os.getpid()}_{gpu}.csv")
+    try:
+        f = open(path, "w")
+        p = subprocess.Popen(["nvidia-smi", "-i", str(gpu), "--query-gpu=" + ",".join(_CLOCK_FIELDS),
+                              "--format=csv,noheader,nounits", "-lms", "200"],
+                             stdout=f, stderr=subprocess.DEVNULL)
+        return p, f, path
+    except OSError:
+        return None
+
+
+def clocks_stop(h):
+    if h is None:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+    p, f, path = h
+    p.terminate()
+    try:
+        p.wait(timeout=5)
+    except subprocess.TimeoutExpired:
+        p.kill()
+    f.close()
+    sm, mx, pw, reasons = [], [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in open(path).read().strip().splitlines():
+        cols = [c.strip() for c in line.split(",")]
+        if len(cols) < 7:
+            continue
+        try:
+            sm.append(float(cols[0]))
+            mx.append(float(cols[1]))
+            pw.append(float(cols[2]))
+        except ValueError:
+            continue
+        for n, v in zip(names, cols[3:7]):
+            if v.lower() == "active":
+                reasons.add(n)
+    os.unlink(path)
+    loaded = [s for s, p_ in zip(sm, pw) if p_ > 300] or sm
+    return {"sm_mhz": statistics.median(loaded) if loaded else None,
+            "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+            "samples": len(sm), "power_w_max": max(pw) if pw else None}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def layer_steps(frames: int) -> int:
+    return (frames // FRAMES_PER_BLOCK) * len(PASSES) * L_
+
+
+def timed_videos(w, args, events: bool):
+    """K videos back to back inside one timed region; returns (ms, per-stage
+    event lists or None)."""
+    import torch
+    n_ls = layer_steps(args.frames)
+    stage = None
+    if events:
+        stage = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
+                 for _ in range(n_ls * args.steps)]
+        cur = [0]
+        w.ctx.on_stage = lambda _name: stage[cur[0]][2].record()
+        hooks = (lambda i: stage[cur[0]][0].record(),
+                 lambda i: stage[cur[0]][1].record(),
+                 lambda i, out: (stage[cur[0]][3].record(), cur.__setitem__(0, cur[0] + 1)))
+    else:
+        hooks = None
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        w.reset()
+        run_video(w, args.frames, hooks=hooks)
+    t1.record()
+    torch.cuda.synchronize()
+    w.ctx.on_stage = None
+    return t0.elapsed_time(t1), stage
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def e2e_videos(w, args, world: int):
+    """Same workload through the public API with host inputs: every layer-step
+    copies its Q/K/V from pinned host memory to the device and its attention
+    output back to pinned host memory, inside the timed region."""
+    import torch
+    host = [tuple(x.cpu().pin_memory() for x in s) for s in w.sets]
+    dq, dk, dv = (torch.empty_like(x) for x in w.sets[0])
+    host_out = torch.empty(tuple(w.sets[0][0].shape), dtype=torch.bfloat16).pin_memory()
+
+    def inputs(i):
+        hq, hk, hv = host[i % N_SETS]
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        return dq, dk, dv
+
+    hooks = (lambda i: None, lambda i: None,
+             lambda i, out: host_out.copy_(out, non_blocking=True))
+    steps = max(1, args.e2e_steps)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        w.reset()
+        run_video(w, args.frames, inputs=inputs, hooks=hooks)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(t0.elapsed_time(t1), world)
+    n_ls = layer_steps(args.frames)
+    per = dq.numel() * 2
+    return {"value": world * steps * args.frames / (ms / 1e3), "unit": "latent frames/s",
+            "h2d_bytes_per_step": 3 * per * n_ls, "d2h_bytes_per_step": per * n_ls,
+            "steps": steps, "ms_per_step": ms / steps,
+            "path": "MegaCache.update/attend with pinned host Q/K/V in and O out per layer-step"}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port of the reference path on the host cores
+# ---------------------------------------------------------------------------
+def cpu_sample(args, budget_s: float = 12.0, warm_blocks: int = 12):
+    """Time one layer-step of the cache path on the CPU oracle at the cache
+    size reached after `warm_blocks` blocks (36 latent frames), layer 0 of the
+    same label matrix: a noisy and a clean update, the plan + pack with RoPE,
+    and the fp32 attention of as many (chunk, head) segments as fit the time
+    budget (scaled to all 36).  Returns (latent frames/s, detail dict)."""
+    import numpy as np
+    from oracle import pkv_oracle as O
+    from pyramidkv import policy
+
+    labels = policy.random_labels(L_, H_, seed=args.seed, merge_fraction=args.merge_fraction)
+    states, caps = policy.states_from_labels(labels[:1], "baseline")
+    tables, _ = O.rope_freq_tables(D_)
+    orc = O.OracleMegaCache(1, H_, D_, FSEQ, 3, 24, 4, states, caps, spatial_width=W_,
+                            sink_time_mapping_mode="window_clamp", sink_time_clamp_min=18,
+                            sink_time_clamp_max=21, freq_tables=tables)
+    rng = np.random.default_rng(args.seed)
+    shape = (1, FRAMES_PER_BLOCK * FSEQ, H_, D_)
+    k, v, q = (O.f32_to_bf16(rng.standard_normal(shape).astype(np.float32)) for _ in range(3))
+    for blk in range(warm_blocks):
+        orc.update(0, k, v, blk * FRAMES_PER_BLOCK * FSEQ, "clean")
+    start = warm_blocks * FRAMES_PER_BLOCK * FSEQ
+    t = time.perf_counter()
+    orc.update(0, k, v, start, "noisy")
+    orc.update(0, k, v, start, "clean")
+    t_update = (time.perf_counter() - t) / 2
+    t = time.perf_counter()
+    pk = orc.plan_and_pack(0, start, FRAMES_PER_BLOCK)
+    t_pack = time.perf_counter() - t
+    kf, vf, cu = O.bf16_to_f32(pk["k"]), O.bf16_to_f32(pk["v"]), pk["cu"]
+    qf = O.bf16_to_f32(q[0])
+    n_seg = FRAMES_PER_BLOCK * H_
+    done, t_attn = 0, 0.0
+    for i in range(n_seg):
+        c, h = divmod(i, H_)
+        t = time.perf_counter()
+        O.attention_fp32(qf[c * FSEQ:(c + 1) * FSEQ, h:h + 1], kf[cu[i]:cu[i + 1]],
+                         vf[cu[i]:cu[i + 1]], np.array([0, cu[i + 1] - cu[i]], np.int32), 1, 1,
+                         FSEQ)
+        t_attn += time.perf_counter() - t
+        done += 1
+        if t_update + t_pack + t_attn > budget_s:
+            break
+    t_attn_all = t_attn * n_seg / done
+    t_ls = t_update + t_pack + t_attn_all
+    fps = args.frames / (layer_steps(args.frames) * t_ls)
+    return fps, {"us_per_layer_step": t_ls * 1e6, "update_s": t_update, "plan_pack_s": t_pack,
+                 "attention_s": t_attn_all, "segments_timed": done, "segments": n_seg,
+                 "kv_tokens": int(pk["total"])}
+
+
+def cpu_baseline_json(fps, detail, cores):
+    return {"value": fps, "unit": "latent frames/s", "cores": cores, "kind": "port",
+            "sample": ("one layer-step of layer 0 at the cache size after 36 latent frames "
+                       f"({detail['kv_tokens']} packed K/V tokens): noisy+clean update, plan+pack "
+                       f"with RoPE, fp32 attention of {detail['segments_timed']}/"
+                       f"{detail['segments']} (chunk, head) segments scaled to all; "
+                       "C restatement single-threaded, attention numpy BLAS on all cores; "
+                       "scaled to 6000 layer-steps per 120-frame video"),
+            "us_per_layer_step": detail["us_per_layer_step"]}
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return
+    cores = os.cpu_count()
+    fps_all = []
+    detail = None
+    for i in range(args.warmup + args.steps):
+        fps, detail = cpu_sample(args, budget_s=4.0)
+        if i >= args.warmup:
+            fps_all.append(fps)
+    fps = statistics.mean(fps_all)
+    line = {"impl": "reference", "metric": METRIC, "value": fps, "unit": "latent frames/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": args.frames / fps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args),
+            "cpu_baseline": cpu_baseline_json(fps, detail, cores),
+            "e2e": {"value": fps, "unit": "latent frames/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": ("the reference path's own CPU code cannot run this workload (its planner "
+                     "needs a CUDA driver and its kernels are CUDA); timed is the oracle port "
+                     "of that path (oracle/pkv_oracle.c + numpy fp32 attention)")}
+    print(json.dumps(line), flush=True)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, \
+            "fallback"
+
+
+def run_ours(args, rank: int, world: int, local: int):
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    w = Workload.build(dev, seed=args.seed + rank, merge_fraction=args.merge_fraction)
+    for _ in range(args.warmup):
+        w.reset()
+        run_video(w, args.frames)
+    torch.cuda.synchronize()
+    if w.ctx.check_status() != 0:
+        raise RuntimeError("device status set during warm-up")
+    w.ctx.token_counter.zero_()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks_start(local)
+    ms, stage = timed_videos(w, args, events=True)
+    clocks = clocks_stop(clk)
+    ms_max = max_over_ranks(ms, world)
+    tokens = int(w.ctx.token_counter.item())
+    n_ls = layer_steps(args.frames)
+    n_total = n_ls * args.steps
+    upd = sum(e[0].elapsed_time(e[1]) for e in stage)
+    pack = sum(e[1].elapsed_time(e[2]) for e in stage)
+    attn = sum(e[2].elapsed_time(e[3]) for e in stage)
+    status = w.ctx.check_status()
+    peaks, peak_kind = measured_peaks()
+    attn_flops = 4.0 * FSEQ * D_ * tokens
+    achieved = attn_flops / (attn / 1e3) / 1e12
+    peak = float(peaks["bf16_tflops_sustained"])
+    pack_bytes = tokens * (2 * D_ * 2 * 2 + 3 * 8 * 2)
+    has_merge = bool(w.ctx.has_merge_head)
+    clean_steps = n_ls // len(PASSES)
+    launches_per_video = n_ls * (2 + 3) + (clean_steps if has_merge else 0)
+    e2e = e2e_videos(w, args, world)
+    fps = world * args.steps * args.frames / (ms_max / 1e3)
+    line = {
+        "metric": METRIC, "value": fps, "unit": "latent frames/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": ("synthetic: seeded N(0,1) bf16 Q/K/V per layer-step, seeded random [30,12] "
+                 "label matrix, model RoPE table; no checkpoint (cache path only)"),
+        "config": workload_config(args),
+        "us_per_layer_step": ms_max * 1e3 / n_total,
+        "breakdown_us_per_layer_step": {"update": upd * 1e3 / n_total,
+                                        "plan_pack": pack * 1e3 / n_total,
+                                        "attention": attn * 1e3 / n_total},
+        "roofline": {"kernel": "attn_tc_kernel (ragged attention, tcgen05/TMEM)",
+                     "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a "
+                                    "long step)",
+                     "frac_of_burst": achieved / float(peaks["bf16_tflops"]),
+                     "flops_per_launch": attn_flops / n_total,
+                     "traffic": None},
+        "pack_roofline": {"bound": "hbm", "unit": "GB/s",
+                          "achieved": pack_bytes / (pack / 1e3) / 1e9,
+                          "peak": float(peaks["hbm_gbs"]),
+                          "frac": pack_bytes / (pack / 1e3) / 1e9 / float(peaks["hbm_gbs"]),
+                          "bytes_per_launch": pack_bytes / n_total},
+        "kv_tokens_per_layer_step": tokens / n_total,
+        "e2e": e2e,
+        "gpu_launches": launches_per_video * args.steps,
+        "clocks": clocks,
+        "device_status": status,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        fps_cpu, detail = cpu_sample(args)
+        line["cpu_baseline"] = cpu_baseline_json(fps_cpu, detail, os.cpu_count())
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

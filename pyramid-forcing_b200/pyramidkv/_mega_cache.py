@@ -71,6 +71,9 @@ class MegaCacheCtx:
     # device int64 counter of packed K/V tokens over all attend calls (the
     # attention FLOP / pack byte accounting of the benchmark); None disables
     token_counter: torch.Tensor = None
+    # optional callable invoked between the pack and the attention launches of
+    # attend() (used to place CUDA events around the attention kernel)
+    on_stage: object = None
 
     def check_status(self) -> int:
         """Synchronise, read and clear the device status word; raise on errors."""
@@ -152,11 +155,18 @@ class MegaCache:
         if softmax_scale is None:
             softmax_scale = D ** -0.5
         counter = ctx.token_counter if ctx.token_counter is not None else _empty_i64(dev)
-        out = _ops.ops().pkv_attend(
-            ctx.mgr, self.states_bytes_for_layer, int(self.layer_idx), q,
-            int(current_start // FSEQ), int(_SINK_MODE.get(ctx.sink_time_mapping_mode, 0)),
-            int(ctx.sink_time_clamp_min), int(ctx.sink_time_clamp_max),
-            int(ctx.decoupled_sink_time_lag), ft, fy, fx, float(softmax_scale), counter)
+        args = (int(current_start // FSEQ), int(_SINK_MODE.get(ctx.sink_time_mapping_mode, 0)),
+                int(ctx.sink_time_clamp_min), int(ctx.sink_time_clamp_max),
+                int(ctx.decoupled_sink_time_lag), ft, fy, fx)
+        ops = _ops.ops()
+        if ctx.on_stage is None:
+            out = ops.pkv_attend(ctx.mgr, self.states_bytes_for_layer, int(self.layer_idx), q,
+                                 *args, float(softmax_scale), counter)
+        else:
+            ops.pkv_attend_pack(ctx.mgr, self.states_bytes_for_layer, int(self.layer_idx),
+                                int(L_q), *args, counter)
+            ctx.on_stage("packed")
+            out = ops.pkv_attend_attention(ctx.mgr, q, float(softmax_scale))
         return out if out.dtype == q.dtype else out.to(q.dtype)
 
 
@@ -217,6 +227,24 @@ def _composition_to_perhead_state(composition) -> ref.PerHeadState:
     return state
 
 
+def _states_from_compositions(compositions, num_layers: int, num_heads: int):
+    """[L][H] compositions -> (uint8 [L, H*600] state bytes, int64 [L, H] sink caps,
+    any merge head)."""
+    size = _mega_state_ops.PER_HEAD_STATE_DTYPE.itemsize
+    raw = np.zeros((num_layers, num_heads * size), dtype=np.uint8)
+    caps = np.zeros((num_layers, num_heads), dtype=np.int64)
+    any_merge = False
+    for l in range(num_layers):
+        if len(compositions[l]) != num_heads:
+            raise ValueError(f"compositions[{l}] has {len(compositions[l])} heads, "
+                             f"expected {num_heads}")
+        states = [_composition_to_perhead_state(c) for c in compositions[l]]
+        any_merge = any_merge or any(s.kind == ref.SK_MERGE for s in states)
+        caps[l] = [int(s.sink_capacity) for s in states]
+        raw[l] = _mega_state_ops.pack_states(states).view(np.uint8).reshape(-1)
+    return raw, caps, any_merge
+
+
 def build_mega_caches(num_layers: int, num_heads: int, head_dim: int, frame_seqlen: int,
                       max_sink_frames: int, max_middle_frames: int, max_recent_frames: int,
                       compositions: Sequence[Sequence], *, max_attend_chunks: int = 8,
@@ -234,19 +262,8 @@ def build_mega_caches(num_layers: int, num_heads: int, head_dim: int, frame_seql
     mgr = torch.classes.adahead.PyramidKVCacheManager(
         num_layers, num_heads, head_dim, frame_seqlen, max_sink_frames, max_middle_frames,
         max_recent_frames, device, kv_dtype, int(max_attend_chunks))
-    per_layer, caps = [], np.zeros((num_layers, num_heads), dtype=np.int64)
-    any_merge = False
-    for l in range(num_layers):
-        if len(compositions[l]) != num_heads:
-            raise ValueError(f"compositions[{l}] has {len(compositions[l])} heads, "
-                             f"expected {num_heads}")
-        states = [_composition_to_perhead_state(c) for c in compositions[l]]
-        any_merge = any_merge or any(s.kind == ref.SK_MERGE for s in states)
-        caps[l] = [int(s.sink_capacity) for s in states]
-        per_layer.append(_mega_state_ops.pack_states(states))
-    raw = np.ascontiguousarray(np.stack(per_layer)).view(np.uint8).reshape(
-        num_layers, num_heads * _mega_state_ops.PER_HEAD_STATE_DTYPE.itemsize)
-    states_bytes = torch.from_numpy(raw.copy()).to(device=device).contiguous()
+    raw, caps, any_merge = _states_from_compositions(compositions, num_layers, num_heads)
+    states_bytes = torch.from_numpy(raw).to(device=device).contiguous()
     parts = flat = None
     if freqs is not None:
         freqs = freqs.to(device=device)

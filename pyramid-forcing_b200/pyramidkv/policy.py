@@ -68,3 +68,44 @@ def random_labels(L: int, H: int, seed: int = 0, merge_fraction: float | None = 
     flat = np.array([-1] * n_merge + [1] * (rest // 2) + [2] * (rest - rest // 2))
     rng.shuffle(flat)
     return flat.reshape(L, H)
+
+
+class _Strategy:
+    """Attribute holder standing in for a reference middle-strategy object;
+    ``_composition_to_perhead_state`` dispatches on the class name."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+class CyclicStrategy(_Strategy):
+    pass
+
+
+class StrideStrategy(_Strategy):
+    pass
+
+
+class MergeStrategy(_Strategy):
+    pass
+
+
+class LabelComposition:
+    """Minimal HeadComposition (sink_frames + middle_strategies) for one head."""
+
+    def __init__(self, label: int, routing: str = "baseline", **kw):
+        st = head_state(label, routing, **kw)
+        self.label = int(label)
+        self.sink_frames = st.sink_capacity
+        if st.kind == ref.SK_CYCLIC:
+            self.middle_strategies = [CyclicStrategy(period=st.period, bucket_cap=st.bucket_cap)]
+        elif st.kind == ref.SK_STRIDE:
+            self.middle_strategies = [StrideStrategy(interval=st.interval, capacity=st.capacity)]
+        else:
+            self.middle_strategies = [MergeStrategy(patch_size=st.patch_size,
+                                                    capacity=st.capacity)]
+
+
+def compositions_from_labels(labels, routing: str = "baseline", **kw):
+    """[L][H] compositions for ``_mega_cache.build_mega_caches``."""
+    return [[LabelComposition(int(x), routing, **kw) for x in row] for row in np.asarray(labels)]

@@ -33,7 +33,7 @@ def _build(cuda, labels, routing, W, Hgrid, D=128, sink_mode="window_clamp"):
     FSEQ = W * Hgrid
     states, caps = policy.states_from_labels(labels, routing)
     (ft, fy, fx), full = O.rope_freq_tables(D)
-    comps = [[_Comp(policy.head_state(int(x), routing)) for x in row] for row in labels]
+    comps = policy.compositions_from_labels(labels, routing)
     caches = _mega_cache.build_mega_caches(
         L, H, D, FSEQ, 3, 24, 4, comps, max_attend_chunks=8, device="cuda:0",
         sink_time_mapping_mode=sink_mode, sink_time_clamp_min=18, sink_time_clamp_max=21,
@@ -44,27 +44,6 @@ def _build(cuda, labels, routing, W, Hgrid, D=128, sink_mode="window_clamp"):
                             rope_mode=O.ROPE_FMA_FIRST)
     np.testing.assert_array_equal(caches[0].ctx.states_bytes.cpu().numpy(), orc.states)
     return caches, orc
-
-
-class _Comp:
-    """Duck-typed HeadComposition carrying an already-built PerHeadState."""
-
-    def __init__(self, st):
-        self._st = st
-        self.sink_frames = st.sink_capacity
-        from pyramidkv import _mega_state_ref as ref
-        kind = st.kind
-        if kind == ref.SK_CYCLIC:
-            self.middle_strategies = [type("CyclicStrategy", (), dict(period=st.period,
-                                                                     bucket_cap=st.bucket_cap))()]
-        elif kind == ref.SK_STRIDE:
-            self.middle_strategies = [type("StrideStrategy", (), dict(interval=st.interval,
-                                                                     capacity=st.capacity))()]
-        elif kind == ref.SK_MERGE:
-            self.middle_strategies = [type("MergeStrategy", (), dict(patch_size=st.patch_size,
-                                                                    capacity=st.capacity))()]
-        else:
-            self.middle_strategies = []
 
 
 def _compare_state(cache, orc, layer, where):

@@ -108,3 +108,16 @@ def test_bf16_rounding_helpers():
     np.testing.assert_array_equal(ours, ref)
     np.testing.assert_array_equal(O.bf16_to_f32(ours),
                                   torch.from_numpy(x).to(torch.bfloat16).float().numpy())
+
+
+def test_build_mega_caches_state_bytes_match_reference_factory():
+    """The state bytes build_mega_caches uploads, for the reference factory's
+    compositions of a 30x12 label matrix (both routings)."""
+    from pyramidkv import _mega_cache, policy
+    g = golden("compositions.npz")
+    for r in ("yaml", "baseline"):
+        comps = policy.compositions_from_labels(g["labels"], r)
+        raw, caps, any_merge = _mega_cache._states_from_compositions(comps, 30, 12)
+        np.testing.assert_array_equal(raw, g[f"{r}_states"])
+        np.testing.assert_array_equal(caps, g[f"{r}_sink_caps"])
+        assert any_merge
