@@ -54,6 +54,11 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--kernel-case", choices=["attn", "pack"], default=None,
+                    help="run one kernel on a standalone steady-state-sized input "
+                         "(small device footprint, for profiler captures) and exit")
+    ap.add_argument("--kernel-iters", type=int, default=4)
     return ap.parse_args()
 
 
@@ -220,11 +225,13 @@ def timed_videos(w, args, events: bool):
     else:
         hooks = None
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     t0.record()
     for _ in range(args.steps):
         w.reset()
         run_video(w, args.frames, hooks=hooks)
     t1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     w.ctx.on_stage = None
     return t0.elapsed_time(t1), stage
@@ -413,7 +420,7 @@ def run_ours(args, rank: int, world: int, local: int):
     has_merge = bool(w.ctx.has_merge_head)
     clean_steps = n_ls // len(PASSES)
     launches_per_video = n_ls * (2 + 3) + (clean_steps if has_merge else 0)
-    e2e = e2e_videos(w, args, world)
+    e2e = None if args.no_e2e else e2e_videos(w, args, world)
     fps = world * args.steps * args.frames / (ms_max / 1e3)
     line = {
         "metric": METRIC, "value": fps, "unit": "latent frames/s", "n_gpus": world,
@@ -452,6 +459,69 @@ def run_ours(args, rank: int, world: int, local: int):
         print(json.dumps(line), flush=True)
 
 
+def run_kernel_case(args):
+    """One kernel on inputs shaped like the C2 steady state: 3 chunks x 12 heads
+    of 1560 queries over per-head KV of 8-14 frames (the plan's mix of sink,
+    recent, middle frames and 390-token merge anchors), ~0.3-0.5 GB on the
+    device.  Prints per-launch time (CUDA events) and the work per launch."""
+    import torch
+    from pyramidkv import _ops, policy
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device="cpu").manual_seed(args.seed)
+    C = FRAMES_PER_BLOCK
+    frames = torch.randint(8, 15, (C * H_,), generator=g)
+    lens = frames * FSEQ + (torch.rand(C * H_, generator=g) < 0.3).long() * 390
+    cu = torch.zeros(C * H_ + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0).int()
+    T = int(cu[-1])
+    ops = _ops.ops()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    if args.kernel_case == "attn":
+        q = torch.randn(1, C * FSEQ, H_, D_, generator=g).to(dev, torch.bfloat16)
+        k = torch.randn(T, D_, generator=g).to(dev, torch.bfloat16)
+        v = torch.randn(T, D_, generator=g).to(dev, torch.bfloat16)
+        cud = cu.to(dev)
+        run = lambda: ops.pkv_attention(q[0], k, v, cud, C, FSEQ, D_ ** -0.5)  # noqa: E731
+        work, unit = 4.0 * FSEQ * D_ * T, "FLOP"
+    else:
+        from pyramidkv import _mega_cache
+        labels = policy.random_labels(1, H_, seed=args.seed)
+        caches = _mega_cache.build_mega_caches(
+            1, H_, D_, FSEQ, 3, 24, 4, policy.compositions_from_labels(labels),
+            device="cuda:0", sink_time_mapping_mode="window_clamp", sink_time_clamp_min=18,
+            sink_time_clamp_max=21, spatial_width=W_, spatial_height=HG_, freqs=rope_table(D_))
+        c = caches[0]
+        shape = (1, C * FSEQ, H_, D_)
+        kk = torch.randn(shape, generator=g).to(dev, torch.bfloat16)
+        for blk in range(30):           # reach a steady-state cache
+            c.update(kk, kk, blk * C * FSEQ, cache_update_mode="clean")
+        ctx = c.ctx
+        start = 30 * C * FSEQ
+        counter = torch.zeros(1, dtype=torch.int64, device=dev)
+        ft, fy, fx = ctx.freq_parts_flat
+        run = lambda: ops.pkv_attend_pack(ctx.mgr, c.states_bytes_for_layer, 0, C * FSEQ,  # noqa
+                                          start // FSEQ, 1, 18, 21, 0, ft, fy, fx, counter)
+        run()
+        torch.cuda.synchronize()
+        tokens = int(counter.item())
+        work, unit = tokens * (2 * D_ * 2 * 2 + 3 * 8 * 2), "B"
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.kernel_iters):
+        ev[0].record()
+        run()
+        ev[1].record()
+        torch.cuda.synchronize()
+        times.append(ev[0].elapsed_time(ev[1]))
+    ms = statistics.median(times)
+    rate = work / (ms / 1e3) / 1e12
+    print(json.dumps({"kernel_case": args.kernel_case, "ms": ms, "work": work, "unit": unit,
+                      "rate": rate, "rate_unit": "T" + unit + "/s"}), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -459,6 +529,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.kernel_case:
+        run_kernel_case(args)
         return
     if world > 1:
         import datetime
