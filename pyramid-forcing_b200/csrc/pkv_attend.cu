@@ -31,7 +31,8 @@ extern "C" int pkv_attend_pack(const pkv_cache_t* c, const uint8_t* states_layer
   int32_t* sg = sk + NMAX;
   int32_t* sln = sg + NMAX;
   int32_t* dst = sln + NMAX;
-  int64_t* traw = reinterpret_cast<int64_t*>(dst + NMAX + (NMAX & 1));
+  // 4 * NMAX int32 precede traw: 16-byte multiple, so traw stays 8-aligned
+  int64_t* traw = reinterpret_cast<int64_t*>(dst + NMAX);
   int64_t* tremap = traw + NMAX;
   int64_t* total = reinterpret_cast<int64_t*>(scr + sl.plan_total);
   int64_t ts[PKV_MAX_CHUNKS];
