@@ -37,6 +37,7 @@ extern "C" {
 #define PKV_ELAUNCH 2    /* the CUDA launch itself failed                    */
 #define PKV_ECAPACITY 3  /* a request cannot fit a compiled or sized bound   */
 #define PKV_EUNSUPPORTED 4
+#define PKV_ENOALLOC_LIMIT 5 /* plan exceeds PKV_NOALLOC_SCRATCH_BYTES        */
 
 /* ---- sticky device status bits ----------------------------------------- */
 #define PKV_ST_PACK_OVERFLOW 0x1   /* plan total > pack workspace capacity   */
@@ -269,6 +270,32 @@ int pkv_attend_attention(const pkv_cache_t *cache, const uint16_t *q, int64_t q_
                          int64_t q_head_stride, int num_chunks, float softmax_scale,
                          uint16_t *out, int64_t o_tok_stride, int64_t o_head_stride,
                          pkv_stream_t stream);
+
+/*
+ * pkv_attend for callers that cannot allocate device memory: a host runtime
+ * that owns the device's memory pool and lends this library only the cache
+ * and each call's inputs and outputs, or a serving loop where a cudaMalloc
+ * could synchronise the device.  Same arguments and results as pkv_attend;
+ * cache->scratch is not used (may be NULL).  The planner's scratch is a fixed
+ * PKV_NOALLOC_SCRATCH_BYTES device array inside libpkv.so, held by every GPU
+ * that loads the library until the process exits.  A call whose plan needs
+ * more -- 32 bytes per segment plus 8, with num_chunks * num_heads *
+ * (max_sink + max_middle + max_recent + max_merge_blocks) segments, i.e. more
+ * than 16383 segments -- returns PKV_ENOALLOC_LIMIT before launching
+ * anything.  The first call on each device looks up the array's device
+ * address; make it before any stream capture.  All calls share the array:
+ * calls whose launches overlap on the GPU race.  No counterpart in the
+ * reference.
+ */
+#define PKV_NOALLOC_SCRATCH_BYTES (512 * 1024)
+int pkv_attend_noalloc(const pkv_cache_t *cache, const uint8_t *states_layer, int layer_idx,
+                       const uint16_t *q, int64_t q_tok_stride, int64_t q_head_stride,
+                       int num_chunks, int64_t first_t, int sink_mode_code, int sink_clamp_min,
+                       int sink_clamp_max, int decoupled_sink_lag, const float *freqs_ft,
+                       int ft_rows, int ft_cols, const float *freqs_fy, int fy_rows, int fy_cols,
+                       const float *freqs_fx, int fx_rows, int fx_cols, float softmax_scale,
+                       uint16_t *out, int64_t o_tok_stride, int64_t o_head_stride,
+                       int64_t *token_counter, pkv_stream_t stream);
 
 /*
  * Evaluation order of the RoPE pair rotation in the pack kernel: 0 =

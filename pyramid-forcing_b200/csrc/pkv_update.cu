@@ -477,6 +477,8 @@ extern "C" const char* pkv_error_string(int code) {
     case PKV_ELAUNCH: return "CUDA launch failed";
     case PKV_ECAPACITY: return "request exceeds a sized or compiled capacity";
     case PKV_EUNSUPPORTED: return "unsupported configuration";
+    case PKV_ENOALLOC_LIMIT:
+      return "plan needs more scratch than the allocation-free entry point's fixed array";
     default: return "unknown error";
   }
 }
