@@ -172,6 +172,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&r)[32]
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31]));
 }
+__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};" ::"r"(addr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -187,6 +195,63 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// ---- paired fp32 arithmetic (sm_100 f32x2: two lanes per instruction) -------
+struct f2 {
+  uint64_t v;
+};
+__device__ __forceinline__ f2 mk2(float lo, float hi) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void un2(f2 a, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(a.v));
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair, on the FMA pipe: Cody-Waite reduction x = n + f with
+// n = rint(x) (the 1.5 * 2^23 addend leaves n in the low mantissa bits) and
+// f in [-0.5, 0.5], a cubic for 2^f, and n added to the exponent field.
+// Cubic coefficients: minimax relative-error fit of 2^f on [-0.5, 0.5]
+// (exp2_poly_fit.py beside this file), max relative error 7.5e-5 -- far below
+// the 2^-8 step of the bf16 P it produces.  x is clamped at -125 so 2^n stays
+// a normal number; such weights are below 2^-125 and vanish in the sums.
+__device__ __forceinline__ f2 exp2_poly2(f2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  un2(x, x0, x1);
+  x = mk2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const f2 t = add2(x, mk2(kRound, kRound));            // n in the low bits of t
+  const f2 r = add2(t, mk2(-kRound, -kRound));          // n as a float
+  float r0, r1;
+  un2(r, r0, r1);
+  const f2 f = add2(x, mk2(-r0, -r1));                  // f = x - n
+  f2 p = fma2(mk2(0.0551716685295105f, 0.0551716685295105f), f,
+              mk2(0.2426111251115799f, 0.2426111251115799f));
+  p = fma2(p, f, mk2(0.6932609677314758f, 0.6932609677314758f));
+  p = fma2(p, f, mk2(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, t0, t1;
+  un2(p, p0, p1);
+  un2(t, t0, t1);
+  // t's bit pattern is 0x4B400000 + n; shifting it left by 23 leaves n << 23
+  const uint32_t e0 = __float_as_uint(t0) << 23, e1 = __float_as_uint(t1) << 23;
+  return mk2(__uint_as_float(__float_as_uint(p0) + e0), __uint_as_float(__float_as_uint(p1) + e1));
 }
 
 // UMMA shared-memory descriptor, 128-byte swizzle (SM100 version bits = 1).
@@ -472,6 +537,373 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Two query tiles per CTA (ping-pong).  One CTA per (segment, pair of 128-row
+// query tiles); both tiles stream the same K/V tiles.  Warp 0: TMA; warp 1:
+// tcgen05.mma issue; warps 2-5: softmax of tile 0; warps 6-9: softmax of
+// tile 1.  TMEM: S0 | S1 | O0 | O1, 128 columns each; P_t overwrites S_t as
+// bf16 pairs.  MMA issue order per K/V tile j:
+//   PV0(j-1)  QK0(j)  PV1(j-1)  QK1(j)
+// so while one softmax warpgroup works on S_t(j) the tensor pipe runs the
+// other tile's P·V and Q·K^T.  The tensor pipe executes one CTA's MMAs in
+// issue order, so QK_t(j) (which overwrites S_t) runs after PV_t(j-1) (which
+// reads P_t from the same columns), and the commit that signals S_t(j) also
+// covers PV_t(j-1): a softmax warpgroup that sees S_t(j) may rescale O_t.
+// Softmax: exp2 of 2 of every 5 column pairs on the FMA pipe (exp2_poly2),
+// the rest on MUFU; the last (partial) K tile uses MUFU only, which maps the
+// masked -inf scores to exactly 0.
+// ---------------------------------------------------------------------------
+constexpr int kThreads2 = 320;
+constexpr int kStages2 = 2;
+
+struct __align__(1024) AttnSmem2 {
+  uint8_t q[2][kTileBytes];
+  uint8_t k[kStages2][kTileBytes];
+  uint8_t v[kStages2][kTileBytes];
+  uint64_t q_full;
+  uint64_t kv_full[kStages2];
+  uint64_t kv_empty[kStages2];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_final[2];
+  uint64_t mma_drain;
+  uint32_t tmem_base;
+  int abort;
+  int seg, unit;
+};
+
+// Row max over 128 raw scores held as bits (tree of 3-input max).
+__device__ __forceinline__ float row_max128(const uint32_t (&s)[4][32]) {
+  float m[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float a[11];
+#pragma unroll
+    for (int i = 0; i < 10; ++i)
+      a[i] = max3(__uint_as_float(s[q][3 * i]), __uint_as_float(s[q][3 * i + 1]),
+                  __uint_as_float(s[q][3 * i + 2]));
+    a[10] = fmaxf(__uint_as_float(s[q][30]), __uint_as_float(s[q][31]));
+    const float b0 = max3(a[0], a[1], a[2]), b1 = max3(a[3], a[4], a[5]);
+    const float b2 = max3(a[6], a[7], a[8]), b3 = fmaxf(a[9], a[10]);
+    m[q] = fmaxf(max3(b0, b1, b2), b3);
+  }
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
+// Which column pairs of a 32-column chunk take the FMA-pipe exp2: 6 of 16.
+__host__ __device__ constexpr bool poly_pair(int i) { return i % 5 == 1 || i % 5 == 3; }
+
+// P for 32 columns (16 pairs) of one row: p = 2^(s * scale - m), summed into
+// two paired accumulators and packed to bf16 pairs.
+template <bool kMixed>
+__device__ __forceinline__ void softmax_chunk(const uint32_t (&s)[32], f2 scale2, f2 negm2,
+                                              f2& acc0, f2& acc1, uint32_t (&pr)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const f2 x = fma2(mk2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), scale2,
+                      negm2);
+    f2 p;
+    if (kMixed && poly_pair(i)) {
+      p = exp2_poly2(x);
+    } else {
+      float x0, x1;
+      un2(x, x0, x1);
+      p = mk2(fast_exp2(x0), fast_exp2(x1));
+    }
+    if (i & 1)
+      acc1 = add2(acc1, p);
+    else
+      acc0 = add2(acc0, p);
+    float p0, p1;
+    un2(p, p0, p1);
+    pr[i] = pack_bf16x2(p0, p1);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads2, 1)
+    attn_tc2_kernel(const __grid_constant__ CUtensorMap tm_q,
+                    const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  AttnSmem2& sm = *reinterpret_cast<AttnSmem2*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  volatile int* abort = &sm.abort;
+  const int units = (a.m_tiles + 1) >> 1;  // query-tile pairs per segment
+  const int order = blockIdx.x / units;
+
+  if (threadIdx.x == 0) {
+    sm.seg = -1;
+    sm.unit = blockIdx.x - order * units;
+    sm.abort = 0;
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_full[t], 4);
+      mbar_init(&sm.o_final[t], 1);
+    }
+    mbar_init(&sm.mma_drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // Longest segments first: the segment whose rank (#segments longer, ties
+  // by index) equals this CTA's order; one thread per candidate segment.
+  for (int s = threadIdx.x; s < a.n_seg; s += blockDim.x) {
+    const int ls = a.cu[s + 1] - a.cu[s];
+    int rank = 0;
+    for (int o = 0; o < a.n_seg; ++o) {
+      const int lo = a.cu[o + 1] - a.cu[o];
+      rank += (lo > ls) || (lo == ls && o < s);
+    }
+    if (rank == order) sm.seg = s;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(&sm.tmem_base)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const int seg = sm.seg;
+  const int unit = sm.unit;
+  const uint32_t tmem = sm.tmem_base;
+  const int c = seg >= 0 ? seg / a.H : 0;
+  const int h = seg >= 0 ? seg - c * a.H : 0;
+  const int kv0 = seg >= 0 ? a.cu[seg] : 0;
+  const int lk = seg >= 0 ? a.cu[seg + 1] - kv0 : 0;
+  const int nkv = (lk + kBN - 1) / kBN;
+  const int ntile = (2 * unit + 1 < a.m_tiles) ? 2 : 1;  // query tiles in this CTA
+  const int row0 = c * a.rows_per_chunk + 2 * unit * kBM;  // global query row of tile 0
+
+  if (seg >= 0 && nkv > 0) {
+    if (warp == 0) {
+      // ---------------- TMA producer ----------------
+      if (lane == 0) {
+        mbar_expect_tx(&sm.q_full, ntile * kTileBytes);
+        for (int t = 0; t < ntile; ++t) {
+          tma_load_3d(sm.q[t], &tm_q, &sm.q_full, 0, h, row0 + t * kBM);
+          tma_load_3d(sm.q[t] + kHalfBytes, &tm_q, &sm.q_full, 64, h, row0 + t * kBM);
+        }
+        int issued = 0;
+        for (int j = 0; j < nkv; ++j) {
+          const int s = j % kStages2;
+          if (j >= kStages2 &&
+              !mbar_wait(&sm.kv_empty[s], ((j / kStages2) + 1) & 1, abort, a.status))
+            break;
+          mbar_expect_tx(&sm.kv_full[s], 2 * kTileBytes);
+          const int y = kv0 + j * kBN;
+          tma_load_2d(sm.k[s], &tm_k, &sm.kv_full[s], 0, y);
+          tma_load_2d(sm.k[s] + kHalfBytes, &tm_k, &sm.kv_full[s], 64, y);
+          tma_load_2d(sm.v[s], &tm_v, &sm.kv_full[s], 0, y);
+          tma_load_2d(sm.v[s] + kHalfBytes, &tm_v, &sm.kv_full[s], 64, y);
+          issued = j + 1;
+        }
+        if (*abort) {
+          // drain this CTA's own copies before the shared memory goes away
+          const uint64_t t0 = now_ns();
+          while (!mbar_try(&sm.q_full, 0) && now_ns() - t0 < kTimeoutNs) {
+          }
+          for (int j = issued > kStages2 ? issued - kStages2 : 0; j < issued; ++j) {
+            const uint64_t t1 = now_ns();
+            while (!mbar_try(&sm.kv_full[j % kStages2], (j / kStages2) & 1) &&
+                   now_ns() - t1 < kTimeoutNs) {
+            }
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      if (lane == 0) {
+        constexpr uint32_t id_qk = idesc_bf16(false);
+        constexpr uint32_t id_pv = idesc_bf16(true);
+        auto issue_qk = [&](int t, int j) {
+          const uint32_t q_s = su32(sm.q[t]);
+          const uint32_t k_s = su32(sm.k[j % kStages2]);
+#pragma unroll
+          for (int kk = 0; kk < kHD / 16; ++kk) {
+            const uint32_t half = (kk >> 2) * kHalfBytes, off = (kk & 3) * 32;
+            mma_ss(tmem + t * 128, sdesc_sw128(q_s + half + off, 16, 1024),
+                   sdesc_sw128(k_s + half + off, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&sm.s_full[t]);
+        };
+        auto issue_pv = [&](int t, int j) {
+          const uint32_t v_s = su32(sm.v[j % kStages2]);
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            // A = P_t (TMEM, 2 bf16 per column), B = V rows kk*16.. (MN-major)
+            mma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                   sdesc_sw128(v_s + kk * 2048, kHalfBytes, 1024), id_pv,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+          }
+        };
+        bool ok = mbar_wait(&sm.q_full, 0, abort, a.status);
+        if (ok) ok = mbar_wait(&sm.kv_full[0], 0, abort, a.status);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < ntile; ++t) issue_qk(t, 0);
+        }
+        for (int j = 0; ok && j < nkv; ++j) {
+          const bool more = j + 1 < nkv;
+          if (!mbar_wait(&sm.p_full[0], j & 1, abort, a.status)) break;
+          tc_fence_after();
+          issue_pv(0, j);
+          if (!more) tc_commit(&sm.o_final[0]);
+          if (more) {
+            const int s1 = (j + 1) % kStages2;
+            if (!mbar_wait(&sm.kv_full[s1], ((j + 1) / kStages2) & 1, abort, a.status)) break;
+            tc_fence_after();
+            issue_qk(0, j + 1);
+          }
+          if (ntile == 2) {
+            if (!mbar_wait(&sm.p_full[1], j & 1, abort, a.status)) break;
+            tc_fence_after();
+            issue_pv(1, j);
+            if (!more) tc_commit(&sm.o_final[1]);
+          }
+          tc_commit(&sm.kv_empty[j % kStages2]);
+          if (ntile == 2 && more) issue_qk(1, j + 1);
+        }
+        // every MMA issued here completes before the CTA frees TMEM
+        tc_commit(&sm.mma_drain);
+        const uint64_t t0 = now_ns();
+        while (!mbar_try(&sm.mma_drain, 0) && now_ns() - t0 < kTimeoutNs) {
+        }
+      }
+    } else {
+      // ---------------- softmax / correction / epilogue of tile t ----------------
+      const int t = (warp - 2) >> 2;
+      if (t < ntile) {
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const uint32_t lane_off = uint32_t(quad * 32) << 16;
+        const uint32_t s_tm = tmem + t * 128 + lane_off;
+        const uint32_t o_tm = tmem + 256 + t * 128 + lane_off;
+        const float sc = a.scale_log2;
+        float m_ref = -INFINITY;  // running reference maximum (log2 domain)
+        float l_sum = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+          if (!mbar_wait(&sm.s_full[t], j & 1, abort, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t sr[4][32];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_ld32(s_tm + q * 32, sr[q]);
+          tmem_wait_ld();
+          const int valid = lk - j * kBN;  // keys of this tile inside the segment
+          const bool partial = valid < kBN;
+          if (partial) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (q * 32 + e >= valid) sr[q][e] = __float_as_uint(-INFINITY);
+          }
+          const float m_new = fmaxf(m_ref, row_max128(sr) * sc);
+          const bool grow = m_new > m_ref + kRescaleThreshold || j == 0;
+          float alpha = 1.0f;
+          if (grow) {
+            alpha = (j == 0) ? 0.0f : fast_exp2(m_ref - m_new);
+            m_ref = m_new;
+          }
+          const f2 scale2 = mk2(sc, sc), negm2 = mk2(-m_ref, -m_ref);
+          f2 acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = mk2(0.0f, 0.0f);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t pr[16];
+            if (partial)
+              softmax_chunk<false>(sr[q], scale2, negm2, acc[2 * q], acc[2 * q + 1], pr);
+            else
+              softmax_chunk<true>(sr[q], scale2, negm2, acc[2 * q], acc[2 * q + 1], pr);
+            tmem_st16(s_tm + q * 16, pr);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i] = add2(acc[i], acc[i + 4]);
+          acc[0] = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+          float r0, r1;
+          un2(acc[0], r0, r1);
+          l_sum = l_sum * alpha + (r0 + r1);
+          // O_t *= alpha for the rows whose reference maximum moved.  S_t(j)
+          // was committed after PV_t(j-1), so O_t is complete here.
+          if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t orr[32];
+              tmem_ld32(o_tm + q * 32, orr);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+              tmem_st32(o_tm + q * 32, orr);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.p_full[t]);
+        }
+        if (ok && mbar_wait(&sm.o_final[t], 0, abort, a.status)) {
+          tc_fence_after();
+          const int grow_row = (2 * unit + t) * kBM + row;
+          const bool store = grow_row < a.rows_per_chunk;
+          const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
+          uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + grow_row) * a.o_row_stride +
+                          int64_t(h) * a.o_head_stride;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t orr[32];
+            tmem_ld32(o_tm + q * 32, orr);
+            tmem_wait_ld();
+            if (store) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 8) {
+                uint4 w;
+                w.x = pack_bf16x2(__uint_as_float(orr[e + 0]) * inv,
+                                  __uint_as_float(orr[e + 1]) * inv);
+                w.y = pack_bf16x2(__uint_as_float(orr[e + 2]) * inv,
+                                  __uint_as_float(orr[e + 3]) * inv);
+                w.z = pack_bf16x2(__uint_as_float(orr[e + 4]) * inv,
+                                  __uint_as_float(orr[e + 5]) * inv);
+                w.w = pack_bf16x2(__uint_as_float(orr[e + 6]) * inv,
+                                  __uint_as_float(orr[e + 7]) * inv);
+                *reinterpret_cast<uint4*>(dst + q * 32 + e) = w;
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (seg >= 0 && warp >= 2) {
+    // empty segment: zero this CTA's output rows
+    const int t = (warp - 2) >> 2;
+    const int grow_row = (2 * unit + t) * kBM + (warp & 3) * 32 + lane;
+    if (t < ntile && grow_row < a.rows_per_chunk) {
+      uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + grow_row) * a.o_row_stride +
+                      int64_t(h) * a.o_head_stride;
+      for (int e = 0; e < kHD; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+// ---------------------------------------------------------------------------
 // CUDA-core path (any even head_dim <= 256): one thread per query row,
 // K/V tiles staged in shared memory, fp32 online softmax.
 // ---------------------------------------------------------------------------
@@ -560,7 +992,7 @@ int launch_attention(const uint16_t* q, int64_t q_rs, int64_t q_hs, const uint16
   if (!q || !k || !v || !cu || !out || num_chunks < 0 || H < 0 || rows_per_chunk < 0 || D <= 0)
     return PKV_EINVAL;
   const int n_seg = num_chunks * H;
-  const bool tc_ok = D == kHD && kv_rows > 0 && kv_rows < (int64_t(1) << 31) &&
+  const bool tc_ok = D == kHD && scale > 0.0f && kv_rows > 0 && kv_rows < (int64_t(1) << 31) &&
                      (reinterpret_cast<uintptr_t>(q) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(k) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(v) % 16 == 0) &&
@@ -590,15 +1022,16 @@ int launch_attention(const uint16_t* q, int64_t q_rs, int64_t q_hs, const uint16
       a.o_row_stride = o_rs;
       a.o_head_stride = o_hs;
       a.status = status;
-      const size_t smem = sizeof(AttnSmem) + 1024;
+      const size_t smem = sizeof(AttnSmem2) + 1024;
       static bool attr_set = false;
       if (!attr_set) {
-        if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(attn_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  int(smem)) != cudaSuccess)
           return PKV_ELAUNCH;
         attr_set = true;
       }
-      attn_tc_kernel<<<n_seg * a.m_tiles, kThreads, smem, stream>>>(mq, mk, mv, a);
+      const int units = (a.m_tiles + 1) / 2;
+      attn_tc2_kernel<<<n_seg * units, kThreads2, smem, stream>>>(mq, mk, mv, a);
       return launch_status();
     }
   }
