@@ -7,21 +7,23 @@
 // from the planner.  Here Q and O are read / written in the caller's
 // [1, L_q, H, D] layout directly, so both permute copies disappear.
 //
-// B200 design (head_dim 128):
-//   * one CTA per (128-row query tile, segment); CTAs are ordered so the
-//     longest segments start first (7x spread of per-head KV lengths) and the
-//     13 query tiles of one segment run side by side, sharing K/V through L2;
-//   * warp 0 issues TMA loads (Q once, K/V 128-row tiles through a 3-stage
-//     ring, 128B-swizzled so the tiles are valid UMMA operands as loaded);
-//   * warp 1 (one elected thread) issues tcgen05.mma: S = Q K^T into one of
-//     two TMEM S buffers, then O += P V with P read from TMEM;
-//   * warps 2-5 (one thread per query row = TMEM lane) run the fp32 online
-//     softmax on S pulled out of TMEM with tcgen05.ld, write P back as bf16
-//     into the S buffer, and rescale O in TMEM only when a row maximum grows by
-//     more than 2^8 (the result is exact: the final O/l uses the same stale
-//     maximum), and normalise and store O at the end;
-//   * every wait is bounded by a wall-clock limit; on expiry the kernel
-//     raises a status bit, drains its own copies, frees TMEM and returns.
+// B200 design (head_dim 128), attn_tc2_kernel:
+//   * one CTA per (segment, pair of 128-row query tiles), 1 CTA per SM;
+//     segments longest first (7x spread of per-head KV lengths), the query
+//     tiles of one segment side by side so they share K/V through L2;
+//   * warp 0 issues TMA loads (both Q tiles once, K/V 128-row tiles through a
+//     2-stage ring, 128B-swizzled so the tiles are valid UMMA operands as
+//     loaded);
+//   * warp 1 (one thread) issues tcgen05.mma for both tiles, interleaved so
+//     the tensor pipe works on one tile while the other is in softmax;
+//   * warps 2-5 and 6-9 (one thread per query row = TMEM lane) run the fp32
+//     online softmax of tile 0 and tile 1 on S pulled out of TMEM with
+//     tcgen05.ld, write P back as bf16 into the S columns, and rescale O in
+//     TMEM only when a row maximum grows by more than 2^8 (exact: the final
+//     O / l uses the same stale maximum); part of each row's exp2 runs as a
+//     polynomial on the FMA pipe to offload the MUFU unit;
+//   * every wait is bounded by a wall-clock limit; on expiry the kernel raises a status bit, drains its own copies
+//     and MMAs, frees TMEM and returns.
 // Other head dims use a plain CUDA-core kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -33,27 +35,10 @@ namespace pkv {
 constexpr int kBM = 128;          // query rows per tile (= TMEM lanes)
 constexpr int kBN = 128;          // keys per tile
 constexpr int kHD = 128;          // head dim of the tensor-core path
-constexpr int kStages = 3;        // K/V ring depth
-constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
 constexpr uint32_t kHalfBytes = kBM * 64 * 2;   // [128 rows][64 bf16] = 16 KB
 constexpr uint32_t kTileBytes = 2 * kHalfBytes; // one 128x128 bf16 tile
 constexpr uint64_t kTimeoutNs = 4000000000ull;  // 4 s per wait
 constexpr float kRescaleThreshold = 8.0f;        // log2 units
-
-struct __align__(1024) AttnSmem {
-  uint8_t q[kTileBytes];
-  uint8_t k[kStages][kTileBytes];
-  uint8_t v[kStages][kTileBytes];
-  uint64_t q_full;
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
-  uint64_t o_done;  // one completion per O += P V
-  uint32_t tmem_base;
-  int abort;
-  int seg, mtile;
-};
 
 // ---- PTX wrappers -----------------------------------------------------------
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -214,6 +199,11 @@ __device__ __forceinline__ f2 add2(f2 a, f2 b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
   return r;
 }
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
 __device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
   f2 r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
@@ -237,11 +227,9 @@ __device__ __forceinline__ f2 exp2_poly2(f2 x) {
   float x0, x1;
   un2(x, x0, x1);
   x = mk2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
-  const f2 t = add2(x, mk2(kRound, kRound));            // n in the low bits of t
-  const f2 r = add2(t, mk2(-kRound, -kRound));          // n as a float
-  float r0, r1;
-  un2(r, r0, r1);
-  const f2 f = add2(x, mk2(-r0, -r1));                  // f = x - n
+  const f2 rnd = mk2(kRound, kRound);
+  const f2 t = add2(x, rnd);                            // n in the low bits of t
+  const f2 f = sub2(x, sub2(t, rnd));                   // f = x - n
   f2 p = fma2(mk2(0.0551716685295105f, 0.0551716685295105f), f,
               mk2(0.2426111251115799f, 0.2426111251115799f));
   p = fma2(p, f, mk2(0.6932609677314758f, 0.6932609677314758f));
@@ -279,263 +267,6 @@ struct AttnArgs {
   int32_t* status;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
-                   const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, AttnArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  AttnSmem& sm = *reinterpret_cast<AttnSmem*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  volatile int* abort = &sm.abort;
-
-  if (threadIdx.x == 0) {
-    // Longest segments first: rank = #segments longer (ties by index).
-    const int order = blockIdx.x / a.m_tiles;
-    int seg = -1;
-    for (int s = 0; s < a.n_seg && seg < 0; ++s) {
-      const int ls = a.cu[s + 1] - a.cu[s];
-      int rank = 0;
-      for (int o = 0; o < a.n_seg; ++o) {
-        const int lo = a.cu[o + 1] - a.cu[o];
-        rank += (lo > ls) || (lo == ls && o < s);
-      }
-      if (rank == order) seg = s;
-    }
-    sm.seg = seg;
-    sm.mtile = blockIdx.x - order * a.m_tiles;
-    sm.abort = 0;
-    mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.s_full[b], 1);
-      mbar_init(&sm.p_full[b], 4);
-    }
-    mbar_init(&sm.o_done, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     su32(&sm.tmem_base)),
-                 "r"(512));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-
-  const int seg = sm.seg;
-  const int mt = sm.mtile;
-  const uint32_t tmem = sm.tmem_base;
-  const int c = seg >= 0 ? seg / a.H : 0;
-  const int h = seg >= 0 ? seg - c * a.H : 0;
-  const int kv0 = seg >= 0 ? a.cu[seg] : 0;
-  const int lk = seg >= 0 ? a.cu[seg + 1] - kv0 : 0;
-  const int nkv = (lk + kBN - 1) / kBN;
-  const int row0 = c * a.rows_per_chunk + mt * kBM;  // global query row of tile row 0
-
-  if (seg >= 0 && nkv > 0) {
-    if (warp == 0) {
-      // ---------------- TMA producer ----------------
-      if (lane == 0) {
-        mbar_expect_tx(&sm.q_full, kTileBytes);
-        tma_load_3d(sm.q, &tm_q, &sm.q_full, 0, h, row0);
-        tma_load_3d(sm.q + kHalfBytes, &tm_q, &sm.q_full, 64, h, row0);
-        int issued = 0;
-        for (int j = 0; j < nkv; ++j) {
-          const int s = j % kStages;
-          if (j >= kStages &&
-              !mbar_wait(&sm.kv_empty[s], ((j / kStages) + 1) & 1, abort, a.status))
-            break;
-          mbar_expect_tx(&sm.kv_full[s], 2 * kTileBytes);
-          const int y = kv0 + j * kBN;
-          tma_load_2d(sm.k[s], &tm_k, &sm.kv_full[s], 0, y);
-          tma_load_2d(sm.k[s] + kHalfBytes, &tm_k, &sm.kv_full[s], 64, y);
-          tma_load_2d(sm.v[s], &tm_v, &sm.kv_full[s], 0, y);
-          tma_load_2d(sm.v[s] + kHalfBytes, &tm_v, &sm.kv_full[s], 64, y);
-          issued = j + 1;
-        }
-        if (*abort) {
-          // drain this CTA's own copies before the shared memory goes away
-          mbar_wait(&sm.q_full, 0, abort, a.status);
-          for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
-            const uint64_t t0 = now_ns();
-            while (!mbar_try(&sm.kv_full[j % kStages], (j / kStages) & 1) &&
-                   now_ns() - t0 < kTimeoutNs) {
-            }
-          }
-        }
-      }
-    } else if (warp == 1) {
-      // ---------------- MMA issuer ----------------
-      if (lane == 0) {
-        constexpr uint32_t id_qk = idesc_bf16(false);
-        constexpr uint32_t id_pv = idesc_bf16(true);
-        const uint32_t s_tm[2] = {tmem, tmem + 128};
-        const uint32_t o_tm = tmem + 256;
-        const uint32_t q_s = su32(sm.q);
-        bool ok = mbar_wait(&sm.q_full, 0, abort, a.status);
-        auto issue_qk = [&](int j) {
-          const int s = j % kStages;
-          const uint32_t k_s = su32(sm.k[s]);
-#pragma unroll
-          for (int kk = 0; kk < kHD / 16; ++kk) {
-            const uint32_t half = (kk >> 2) * kHalfBytes, off = (kk & 3) * 32;
-            mma_ss(s_tm[j & 1], sdesc_sw128(q_s + half + off, 16, 1024),
-                   sdesc_sw128(k_s + half + off, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
-          }
-          tc_commit(&sm.s_full[j & 1]);
-        };
-        if (ok) ok = mbar_wait(&sm.kv_full[0], 0, abort, a.status);
-        if (ok) {
-          tc_fence_after();
-          issue_qk(0);
-        }
-        for (int j = 0; ok && j < nkv; ++j) {
-          if (j + 1 < nkv) {
-            const int s1 = (j + 1) % kStages;
-            if (!mbar_wait(&sm.kv_full[s1], ((j + 1) / kStages) & 1, abort, a.status)) break;
-            tc_fence_after();
-            issue_qk(j + 1);
-          }
-          if (!mbar_wait(&sm.p_full[j & 1], (j >> 1) & 1, abort, a.status)) break;
-          tc_fence_after();
-          const uint32_t v_s = su32(sm.v[j % kStages]);
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            // A = P (TMEM, 2 bf16 per column), B = V rows kk*16.. (MN-major)
-            mma_ts(o_tm, s_tm[j & 1] + kk * 8, sdesc_sw128(v_s + kk * 2048, kHalfBytes, 1024),
-                   id_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(&sm.kv_empty[j % kStages]);
-          tc_commit(&sm.o_done);
-        }
-      }
-    } else {
-      // ---------------- softmax / correction / epilogue ----------------
-      const int quad = warp & 3;
-      const int row = quad * 32 + lane;
-      const uint32_t lane_off = uint32_t(quad * 32) << 16;
-      const uint32_t o_tm = tmem + 256 + lane_off;
-      float m_ref = -INFINITY;  // running reference maximum (log2 domain)
-      float l_sum = 0.0f;
-      bool ok = true;
-      for (int j = 0; j < nkv; ++j) {
-        const uint32_t s_tm = tmem + (j & 1) * 128 + lane_off;
-        if (!mbar_wait(&sm.s_full[j & 1], (j >> 1) & 1, abort, a.status)) { ok = false; break; }
-        tc_fence_after();
-        uint32_t sr[4][32];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) tmem_ld32(s_tm + q * 32, sr[q]);
-        tmem_wait_ld();
-        const int valid = lk - j * kBN;  // keys of this tile inside the segment
-        float mx = -INFINITY;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x = (q * 32 + e < valid) ? __uint_as_float(sr[q][e]) * a.scale_log2
-                                                 : -INFINITY;
-            sr[q][e] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
-          }
-        const float m_new = fmaxf(m_ref, mx);
-        const bool grow = m_new > m_ref + kRescaleThreshold || j == 0;
-        float alpha = 1.0f;
-        if (grow) {
-          alpha = (j == 0) ? 0.0f : fast_exp2(m_ref - m_new);
-          m_ref = m_new;
-        }
-        float rs = 0.0f;
-        uint32_t pr[2][32];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float p0 = fast_exp2(__uint_as_float(sr[q][e]) - m_ref);
-            const float p1 = fast_exp2(__uint_as_float(sr[q][e + 1]) - m_ref);
-            rs += p0 + p1;
-            pr[q >> 1][(q & 1) * 16 + (e >> 1)] = pack_bf16x2(p0, p1);
-          }
-        l_sum = l_sum * alpha + rs;
-        tmem_st32(s_tm, pr[0]);
-        tmem_st32(s_tm + 32, pr[1]);
-        // O += P_{j-1} V_{j-1} must be complete before P_j is released (and
-        // before O is rescaled).  Waiting for every completion in order keeps
-        // the parity of this barrier exact.
-        if (j > 0) {
-          if (!mbar_wait(&sm.o_done, (j - 1) & 1, abort, a.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-        }
-        // O *= alpha for the rows whose reference maximum moved (warp-wide op)
-        if (j > 0 && __any_sync(0xffffffffu, grow)) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t orr[32];
-            tmem_ld32(o_tm + q * 32, orr);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-            tmem_st32(o_tm + q * 32, orr);
-          }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.p_full[j & 1]);
-      }
-      if (ok && mbar_wait(&sm.o_done, (nkv - 1) & 1, abort, a.status)) {
-        tc_fence_after();
-        const int grow_row = mt * kBM + row;
-        const bool store = grow_row < a.rows_per_chunk;
-        const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
-        uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + grow_row) * a.o_row_stride +
-                        int64_t(h) * a.o_head_stride;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t orr[32];
-          tmem_ld32(o_tm + q * 32, orr);
-          tmem_wait_ld();
-          if (store) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 8) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(orr[e + 0]) * inv, __uint_as_float(orr[e + 1]) * inv);
-              w.y = pack_bf16x2(__uint_as_float(orr[e + 2]) * inv, __uint_as_float(orr[e + 3]) * inv);
-              w.z = pack_bf16x2(__uint_as_float(orr[e + 4]) * inv, __uint_as_float(orr[e + 5]) * inv);
-              w.w = pack_bf16x2(__uint_as_float(orr[e + 6]) * inv, __uint_as_float(orr[e + 7]) * inv);
-              *reinterpret_cast<uint4*>(dst + q * 32 + e) = w;
-            }
-          }
-        }
-      }
-    }
-  } else if (seg >= 0 && warp >= 2) {
-    // empty segment: zero output rows
-    const int row = (warp & 3) * 32 + lane;
-    const int grow_row = mt * kBM + row;
-    if (grow_row < a.rows_per_chunk) {
-      uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + grow_row) * a.o_row_stride +
-                      int64_t(h) * a.o_head_stride;
-      for (int e = 0; e < kHD; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 0) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Two query tiles per CTA (ping-pong).  One CTA per (segment, pair of 128-row
 // query tiles); both tiles stream the same K/V tiles.  Warp 0: TMA; warp 1:
@@ -554,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 constexpr int kThreads2 = 320;
 constexpr int kStages2 = 2;
+constexpr int kMaxSegLens = 1024;  // segment lengths staged in shared memory
 
 struct __align__(1024) AttnSmem2 {
   uint8_t q[2][kTileBytes];
@@ -569,6 +301,7 @@ struct __align__(1024) AttnSmem2 {
   uint32_t tmem_base;
   int abort;
   int seg, unit;
+  int seg_len[kMaxSegLens];
 };
 
 // Row max over 128 raw scores held as bits (tree of 3-input max).
@@ -628,12 +361,16 @@ __global__ void __launch_bounds__(kThreads2, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort = &sm.abort;
-  const int units = (a.m_tiles + 1) >> 1;  // query-tile pairs per segment
+  // Segment-major: the units of one segment are adjacent CTAs, so they run
+  // side by side and read its K/V from HBM once (scheduling the odd last
+  // tiles after all pairs measured slower: their K/V had left L2).
+  const int units = (a.m_tiles + 1) >> 1;
   const int order = blockIdx.x / units;
+  const int unit_of_block = blockIdx.x - order * units;
 
   if (threadIdx.x == 0) {
     sm.seg = -1;
-    sm.unit = blockIdx.x - order * units;
+    sm.unit = unit_of_block;
     sm.abort = 0;
     mbar_init(&sm.q_full, 1);
     for (int s = 0; s < kStages2; ++s) {
@@ -648,14 +385,18 @@ __global__ void __launch_bounds__(kThreads2, 1)
     mbar_init(&sm.mma_drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncthreads();
   // Longest segments first: the segment whose rank (#segments longer, ties
-  // by index) equals this CTA's order; one thread per candidate segment.
+  // by index) equals this CTA's order; one thread per candidate segment,
+  // lengths staged in shared memory when they fit.
+  const bool lens_in_smem = a.n_seg <= kMaxSegLens;
+  if (lens_in_smem)
+    for (int s = threadIdx.x; s < a.n_seg; s += blockDim.x) sm.seg_len[s] = a.cu[s + 1] - a.cu[s];
+  __syncthreads();
   for (int s = threadIdx.x; s < a.n_seg; s += blockDim.x) {
-    const int ls = a.cu[s + 1] - a.cu[s];
+    const int ls = lens_in_smem ? sm.seg_len[s] : a.cu[s + 1] - a.cu[s];
     int rank = 0;
     for (int o = 0; o < a.n_seg; ++o) {
-      const int lo = a.cu[o + 1] - a.cu[o];
+      const int lo = lens_in_smem ? sm.seg_len[o] : a.cu[o + 1] - a.cu[o];
       rank += (lo > ls) || (lo == ls && o < s);
     }
     if (rank == order) sm.seg = s;
