@@ -35,6 +35,7 @@ for _p in (ROOT, os.path.join(ROOT, "pyramid-forcing_b200")):
         sys.path.insert(0, _p)
 
 METRIC = "cache-update+ragged-attn µs per DiT layer-step; latent frames/sec"
+ATTN_DRAM_BYTES_PER_FLOP = 351.1e6 / 492.171264e9  # ncu capture, attn kernel case
 L_, H_, D_, W_, HG_ = 30, 12, 128, 52, 30
 FSEQ = W_ * HG_
 FRAMES_PER_BLOCK = 3
@@ -433,14 +434,18 @@ def run_ours(args, rank: int, world: int, local: int):
         "breakdown_us_per_layer_step": {"update": upd * 1e3 / n_total,
                                         "plan_pack": pack * 1e3 / n_total,
                                         "attention": attn * 1e3 / n_total},
-        "roofline": {"kernel": "attn_tc_kernel (ragged attention, tcgen05/TMEM)",
+        "roofline": {"kernel": "attn_tc2_kernel (ragged attention, tcgen05/TMEM)",
                      "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak,
                      "peak_source": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a "
                                     "long step)",
                      "frac_of_burst": achieved / float(peaks["bf16_tflops"]),
                      "flops_per_launch": attn_flops / n_total,
-                     "traffic": None},
+                     # DRAM bytes per launch: one ncu capture of the kernel case
+                     # (profiles/attn_tc2_kernel_steady_state.md), scaled by work
+                     "traffic": ATTN_DRAM_BYTES_PER_FLOP * attn_flops / n_total,
+                     "traffic_source": "ncu dram__bytes_read+write of the kernel case "
+                                       "(351.1 MB / 0.492 TFLOP), scaled to this launch"},
         "pack_roofline": {"bound": "hbm", "unit": "GB/s",
                           "achieved": pack_bytes / (pack / 1e3) / 1e9,
                           "peak": float(peaks["hbm_gbs"]),

@@ -22,8 +22,9 @@
 //     TMEM only when a row maximum grows by more than 2^8 (exact: the final
 //     O / l uses the same stale maximum); part of each row's exp2 runs as a
 //     polynomial on the FMA pipe to offload the MUFU unit;
-//   * every wait is bounded by a wall-clock limit; on expiry the kernel raises a status bit, drains its own copies
-//     and MMAs, frees TMEM and returns.
+//   * every wait is bounded by a wall-clock limit; on expiry the kernel
+//     raises a status bit, drains its own copies and MMAs, frees TMEM and
+//     returns.
 // Other head dims use a plain CUDA-core kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
