@@ -87,7 +87,7 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) {
 }
 
 // Round-to-nearest-even f32 -> bf16 bits (the conversion __float2bfloat16
-// performs), done with integer ops so it is exact and NaN-preserving.
+// performs).
 __device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
   const __nv_bfloat16 h = __float2bfloat16_rn(f);
   return static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&h));

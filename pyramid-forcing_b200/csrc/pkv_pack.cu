@@ -171,6 +171,290 @@ __global__ void __launch_bounds__(256) pack_kernel(PackArgs a) {
   }
 }
 
+constexpr int kPack128MaxSeg = 2048;  // plans with more segments use pack_kernel
+
+// ---------------------------------------------------------------------------
+// pack_bulk_kernel (head_dim 128): tiles of 64 tokens staged through shared
+// memory by bulk async copies.  One thread per block keeps a 2-stage ring of
+// (K, V, positions) tiles in flight with cp.async.bulk global -> shared (no
+// multicast); V goes straight back out with a bulk shared -> global store; the
+// block's threads read K (and positions) from shared memory, rotate and store
+// K and copy the positions.  A block holds up to 2 x 33.5 KB in flight without
+// spending registers on it, which a gather-copy needs to approach HBM rate.
+// ---------------------------------------------------------------------------
+constexpr int kBulkTok = 64;
+constexpr int kBulkStages = 2;
+constexpr int kBulkThreads = 256;
+constexpr uint64_t kBulkTimeoutNs = 4000000000ull;
+
+struct __align__(128) BulkStage {
+  uint16_t k[kBulkTok * 128];
+  uint16_t v[kBulkTok * 128];
+  int64_t pos[kBulkTok * 3];
+};
+struct BulkTileMeta {
+  int64_t dst0;      // packed row of the segment's first token
+  int64_t src_row;   // pool row of the tile's first token
+  int64_t tm;        // remapped time (>= 0) or -1
+  int tok0, ntok, kind;
+  int bad;           // segment failed its bounds checks: skip
+  int pos_in_smem;   // positions arrived with the bulk copy
+};
+struct BulkSmem {
+  BulkStage st[kBulkStages];
+  uint64_t full[kBulkStages];
+  BulkTileMeta meta[kBulkStages];
+  int tile_start[kPack128MaxSeg + 1];
+  int warp_tot[kBulkThreads / 32];
+};
+
+// Row r of a table with `rows` rows, clamped into [0, rows) (rows >= 1).
+__device__ __forceinline__ int clamp_row(int64_t r, int rows) {
+  if (static_cast<uint64_t>(r) < static_cast<uint64_t>(rows)) return static_cast<int>(r);
+  return r < 0 ? 0 : rows - 1;
+}
+// Two f32 -> one bf16 pair (lo, hi), each rounded to nearest even: the same
+// bits as two f32_to_bf16_bits conversions, in one instruction.
+__device__ __forceinline__ uint32_t pack_bf16_pair(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pk_smem(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t pk_now() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool pk_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(pk_smem(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait on a stage; false after kBulkTimeoutNs
+__device__ __forceinline__ bool pk_wait(uint64_t* b, uint32_t parity) {
+  if (pk_try(b, parity)) return true;
+  const uint64_t t0 = pk_now();
+  while (!pk_try(b, parity))
+    if (pk_now() - t0 > kBulkTimeoutNs) return false;
+  return true;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(pk_smem(dst)), "l"(src), "r"(bytes), "r"(pk_smem(b))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               ::"l"(dst), "r"(pk_smem(src)), "r"(bytes)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a) {
+  extern __shared__ uint8_t pk_raw[];
+  BulkSmem& sm = *reinterpret_cast<BulkSmem*>(
+      (reinterpret_cast<uintptr_t>(pk_raw) + 127) & ~uintptr_t(127));
+  const int n = a.n_seg;
+  // ---- compact tile list (as pack128_kernel)
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int s_begin = min(n, int(threadIdx.x) * per), s_end = min(n, s_begin + per);
+  int run = 0;
+  for (int sg = s_begin; sg < s_end; ++sg) {
+    const int kind = a.sk[sg], len = a.sl[sg];
+    int nt = 0;
+    if (kind >= 0 && len > 0) {
+      if (kind > 3) {
+        if (blockIdx.x == 0) flag(a.status, PKV_ST_BAD_KIND);
+      } else {
+        nt = (len + kBulkTok - 1) / kBulkTok;
+      }
+    }
+    sm.tile_start[sg] = nt;
+    run += nt;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) sm.warp_tot[warp] = incl;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kBulkStages; ++st)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(pk_smem(&sm.full[st])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  int before = 0, total = 0;
+  for (int w = 0; w < int(blockDim.x >> 5); ++w) {
+    if (w < warp) before += sm.warp_tot[w];
+    total += sm.warp_tot[w];
+  }
+  int acc = before + incl - run;
+  for (int sg = s_begin; sg < s_end; ++sg) {
+    const int nt = sm.tile_start[sg];
+    sm.tile_start[sg] = acc;
+    acc += nt;
+  }
+  if (threadIdx.x == 0) sm.tile_start[n] = total;
+  __syncthreads();
+
+  const int per_block = (total + int(gridDim.x) - 1) / int(gridDim.x);
+  const int u_begin = min(total, int(blockIdx.x) * per_block);
+  const int count = min(total, u_begin + per_block) - u_begin;
+  if (count <= 0) return;
+
+  // ---- producer (thread 0): tile i -> stage i % kBulkStages
+  int iseg = 0;
+  if (threadIdx.x == 0) {
+    int lo = 0, hi = n;  // tile_start[lo] <= u_begin < tile_start[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (sm.tile_start[mid] <= u_begin) lo = mid; else hi = mid;
+    }
+    iseg = lo;
+  }
+  auto issue = [&](int i) {
+    const int u = u_begin + i;
+    while (sm.tile_start[iseg + 1] <= u) ++iseg;
+    const int st = i % kBulkStages;
+    BulkTileMeta& m = sm.meta[st];
+    const int kind = a.sk[iseg], len = a.sl[iseg];
+    const int64_t slot = a.sg[iseg], dst0 = a.dst[iseg];
+    const int stride_tok = kind == kSrcMerge ? a.MTPA : a.F;
+    const int tok0 = (u - sm.tile_start[iseg]) * kBulkTok;
+    m.kind = kind;
+    m.tok0 = tok0;
+    m.ntok = min(kBulkTok, len - tok0);
+    m.dst0 = dst0;
+    m.bad = slot < 0 || slot >= a.rows[kind] || len > stride_tok || dst0 < 0 ||
+            dst0 + len > a.out_rows || a.k[kind] == nullptr;
+    uint64_t* bar = &sm.full[st];
+    if (m.bad) {
+      if (tok0 == 0)
+        flag(a.status, dst0 + len > a.out_rows ? PKV_ST_PACK_OVERFLOW : PKV_ST_SLOT_RANGE);
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pk_smem(bar)) : "memory");
+      return;
+    }
+    m.src_row = slot * stride_tok + tok0;
+    m.tm = (a.rope && a.pos[kind] != nullptr) ? a.tremap[iseg] : -1;
+    // 16-byte rule of the bulk copy: 24 * src_row and 24 * ntok must be multiples of 16
+    m.pos_in_smem = a.pos[kind] != nullptr && (m.src_row & 1) == 0 && (m.ntok & 1) == 0;
+    const uint32_t kv_bytes = uint32_t(m.ntok) * 256;
+    const uint32_t pos_bytes = m.pos_in_smem ? uint32_t(m.ntok) * 24 : 0;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(pk_smem(bar)),
+                 "r"(2 * kv_bytes + pos_bytes)
+                 : "memory");
+    bulk_g2s(sm.st[st].k, a.k[kind] + m.src_row * 128, kv_bytes, bar);
+    bulk_g2s(sm.st[st].v, a.v[kind] + m.src_row * 128, kv_bytes, bar);
+    if (pos_bytes) bulk_g2s(sm.st[st].pos, a.pos[kind] + m.src_row * 3, pos_bytes, bar);
+  };
+  int issued = 0;
+  if (threadIdx.x == 0)
+    for (; issued < min(kBulkStages, count); ++issued) issue(issued);
+
+  // ---- this thread's four complex pairs are fixed: resolve their tables once
+  const int ch = threadIdx.x & 15;
+  const float2* ftab[4];
+  int fcols[4], fsel[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int pp = ch * 4 + j;
+    const float* tab;
+    int col;
+    if (pp < a.ft_cols) {
+      tab = a.ft; fcols[j] = a.ft_cols; col = pp; fsel[j] = 0;
+    } else if (pp < a.ft_cols + a.fy_cols) {
+      tab = a.fy; fcols[j] = a.fy_cols; col = pp - a.ft_cols; fsel[j] = 1;
+    } else {
+      tab = a.fx; fcols[j] = a.fx_cols; col = pp - a.ft_cols - a.fy_cols; fsel[j] = 2;
+    }
+    ftab[j] = tab ? reinterpret_cast<const float2*>(tab) + col : nullptr;
+  }
+  const int rope_mode = a.rope_mode;
+
+  int done = 0;
+  for (int i = 0; i < count; ++i) {
+    const int st = i % kBulkStages;
+    const bool ok = pk_wait(&sm.full[st], uint32_t(i / kBulkStages) & 1u);
+    if (__syncthreads_or(!ok)) {  // block-uniform: every thread leaves together
+      if (threadIdx.x == 0) flag(a.status, PKV_ST_TIMEOUT);
+      break;
+    }
+    const BulkTileMeta m = sm.meta[st];
+    if (!m.bad) {
+      const BulkStage& sb = sm.st[st];
+      const int64_t drow = m.dst0 + m.tok0;
+      if (threadIdx.x == 0) {
+        bulk_s2g(a.v_out + drow * 128, sb.v, uint32_t(m.ntok) * 256);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+      const bool has_pos = a.pos[m.kind] != nullptr;
+      const bool rope = a.rope && has_pos;
+      const int64_t* gpos = has_pos ? a.pos[m.kind] + m.src_row * 3 : nullptr;
+#pragma unroll
+      for (int q = 0; q < (kBulkTok * 16) / kBulkThreads; ++q) {
+        const int r = (int(threadIdx.x) + kBulkThreads * q) >> 4;
+        if (r >= m.ntok) continue;
+        uint4 kk = *reinterpret_cast<const uint4*>(sb.k + r * 128 + ch * 8);
+        if (rope) {
+          int64_t pt, py, px;
+          if (m.pos_in_smem) {
+            pt = sb.pos[r * 3]; py = sb.pos[r * 3 + 1]; px = sb.pos[r * 3 + 2];
+          } else {
+            pt = __ldg(gpos + r * 3); py = __ldg(gpos + r * 3 + 1); px = __ldg(gpos + r * 3 + 2);
+          }
+          if (m.tm >= 0) pt = m.tm;
+          // table rows of this token, clamped once per coordinate
+          const int rt = clamp_row(pt, a.ft_rows), ry = clamp_row(py, a.fy_rows);
+          const int rx = clamp_row(px, a.fx_rows);
+          uint32_t w[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float2 fq = make_float2(1.0f, 0.0f);
+            if (ftab[j] != nullptr)
+              fq = __ldg(ftab[j] + (fsel[j] == 0 ? rt : fsel[j] == 1 ? ry : rx) * fcols[j]);
+            const float kr = bf16_bits_to_f32(w[j] & 0xffffu);
+            const float ki = bf16_bits_to_f32(w[j] >> 16);
+            float nr, ni;
+            rotate(kr, ki, fq.x, fq.y, rope_mode, nr, ni);
+            w[j] = pack_bf16_pair(nr, ni);
+          }
+          kk = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        *reinterpret_cast<uint4*>(a.k_out + (drow + r) * 128 + ch * 8) = kk;
+      }
+      if (a.pos_out != nullptr && has_pos) {
+        int64_t* dp = a.pos_out + drow * 3;
+        for (int e = threadIdx.x; e < m.ntok * 3; e += blockDim.x)
+          dp[e] = m.pos_in_smem ? sb.pos[e] : __ldg(gpos + e);
+      }
+    }
+    __syncthreads();  // every read of stage st is done
+    done = i + 1;
+    if (threadIdx.x == 0 && issued < count) {
+      // the V store of this stage must have read its shared memory
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      issue(issued++);
+    }
+  }
+  if (threadIdx.x == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    // on a timeout, let this block's own copies land before shared memory goes
+    for (int i = done; i < issued; ++i) pk_wait(&sm.full[i % kBulkStages], uint32_t(i / kBulkStages) & 1u);
+  }
+}
+
 int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, const int32_t* sl,
                 const int32_t* dst, int n_seg, const int64_t* tremap, const float* ft,
                 int ft_rows, int ft_cols, const float* fy, int fy_rows, int fy_cols,
@@ -213,8 +497,29 @@ int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, cons
   bool vec = (a.D % 8 == 0);
   for (int i = 0; i < 4; ++i)
     vec = vec && ((reinterpret_cast<uintptr_t>(a.k[i]) | reinterpret_cast<uintptr_t>(a.v[i])) % 16 == 0);
-  if (vec) pack_kernel<true><<<int(grid), 256, 0, stream>>>(a);
-  else pack_kernel<false><<<int(grid), 256, 0, stream>>>(a);
+  const bool bulk_ok =
+      vec && a.D == 128 && n_seg <= kPack128MaxSeg &&
+      ((reinterpret_cast<uintptr_t>(a.k_out) | reinterpret_cast<uintptr_t>(a.v_out)) % 16 == 0) &&
+      ((reinterpret_cast<uintptr_t>(a.pos[0]) | reinterpret_cast<uintptr_t>(a.pos[1]) |
+        reinterpret_cast<uintptr_t>(a.pos[2]) | reinterpret_cast<uintptr_t>(a.pos[3])) % 16 == 0);
+  if (bulk_ok) {
+    // a persistent grid of exactly the resident blocks
+    static int per_sm = 0;
+    const int smem = int(sizeof(BulkSmem)) + 128;
+    if (per_sm == 0) {
+      if (cudaFuncSetAttribute(pack_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess ||
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pack_bulk_kernel, kBulkThreads, smem) !=
+              cudaSuccess)
+        return PKV_ELAUNCH;
+      if (per_sm < 1) per_sm = 1;
+    }
+    pack_bulk_kernel<<<sm_count() * per_sm, kBulkThreads, smem, stream>>>(a);
+  } else if (vec) {
+    pack_kernel<true><<<int(grid), 256, 0, stream>>>(a);
+  } else {
+    pack_kernel<false><<<int(grid), 256, 0, stream>>>(a);
+  }
   return launch_status();
 }
 
