@@ -297,6 +297,47 @@ int pkv_attend_noalloc(const pkv_cache_t *cache, const uint8_t *states_layer, in
                        uint16_t *out, int64_t o_tok_stride, int64_t o_head_stride,
                        int64_t *token_counter, pkv_stream_t stream);
 
+/* ---- AdaptiveKVCache / CppStrategyManager ops (not on the MegaCache path) ----
+ * Same bytes as the reference's kernels; launched on `stream` (the
+ * reference's use the legacy default stream).  One CTA per segment / frame.
+ */
+
+/* dst + offsets[s] * row_bytes <- lengths[s] rows of row_bytes bytes from the
+ * device address src_ptrs[s], for each s < num_segments.
+ * Replaces: scatter_copy (pyramidkv/csrc/scatter_copy.cu:13-47, :230-248). */
+int pkv_scatter_copy(const int64_t *src_ptrs, const int64_t *lengths, const int64_t *offsets,
+                     void *dst, int64_t row_bytes, int num_segments, pkv_stream_t stream);
+
+/* pos[i * 3] = vals[r] for starts[r] <= i < ends[r], r < num_ranges.
+ * Replaces: apply_pos_override (scatter_copy.cu:53-71, :250-267). */
+int pkv_pos_override(int64_t *pos, const int64_t *starts, const int64_t *ends,
+                     const int64_t *vals, int num_ranges, pkv_stream_t stream);
+
+/* Copy segment s (lengths[s] rows, device addresses src_ptrs_k/v/pos[s]) to
+ * rows offsets[s].. of dst_k / dst_v / dst_rope_pos, remapping each row's
+ * time: flags bit 2 -> dynamic_rope_t[s]; else bit 0 -> history mapping
+ * (mapping_mode 1 relative_clamp, 2 relative_softcap, 0 none) against
+ * current_t; dst_frame_ids gets the stored time when flags bit 1 is set, else
+ * the mapped one.  Replaces: refresh_readout_layout (scatter_copy.cu:77-168,
+ * scatter_copy_bind.cpp:483-627). */
+int pkv_refresh_readout_layout(const int64_t *src_ptrs_k, const int64_t *src_ptrs_v,
+                               const int64_t *src_ptrs_pos, const int64_t *offsets,
+                               const int64_t *lengths, const int64_t *flags,
+                               const int64_t *dynamic_rope_t, void *dst_k, void *dst_v,
+                               int64_t *dst_rope_pos, int64_t *dst_frame_ids, int64_t row_bytes,
+                               int64_t current_t, int mapping_mode,
+                               int64_t history_relative_t_max, float history_time_soft_factor,
+                               int num_segments, pkv_stream_t stream);
+
+/* Frame f with frame_desc[f] = (src_frame, slot), both >= 0: copy frame
+ * src_frame of k_seq / v_seq / pos_seq (frame_seqlen rows) into store slot
+ * `slot`.  Replaces: anchor_store_write_frames (scatter_copy.cu:170-225,
+ * scatter_copy_bind.cpp:630-684). */
+int pkv_anchor_store_write_frames(const void *k_seq, const void *v_seq, const int64_t *pos_seq,
+                                  const int64_t *frame_desc, void *store_k, void *store_v,
+                                  int64_t *store_pos, int64_t frame_seqlen, int64_t row_bytes,
+                                  int num_frames, pkv_stream_t stream);
+
 /*
  * Evaluation order of the RoPE pair rotation in the pack kernel: 0 =
  * fma(kr, fr, -(ki*fi)) / fma(kr, fi, ki*fr) (default), 1 = fma on the second

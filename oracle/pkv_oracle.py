@@ -464,3 +464,64 @@ def make_states(kinds_params, H=None) -> np.ndarray:
         # merge_active_block_id @568 -> idx 141 (2)
         i32[141:143] = -1
     return buf
+
+
+# ---------------------------------------------------------------------------
+# AdaptiveKVCache / CppStrategyManager ops (pyramidkv/csrc/scatter_copy.cu)
+# ---------------------------------------------------------------------------
+def legacy_map_t(src_t: int, current_t: int, mode: int, rel_max: int, soft: float) -> int:
+    """History time mapping of one stored time (scatter_copy.cu:138-163):
+    mode 1 clamps current_t - t at rel_max, mode 2 compresses the excess by
+    ``soft`` (float32 product rounded to nearest even, as llrintf); never < 0."""
+    if rel_max <= 0:
+        return int(src_t)
+    rel = max(int(current_t) - int(src_t), 0)
+    t = int(src_t)
+    if mode == 1:
+        rel = min(rel, int(rel_max))
+        t = int(current_t) - rel
+    elif mode == 2:
+        if rel > rel_max:
+            rel = int(rel_max) + int(np.rint(np.float32(rel - rel_max) * np.float32(soft)))
+        t = int(current_t) - rel
+    return max(t, 0)
+
+
+def legacy_refresh(srcs_k, srcs_v, srcs_pos, offsets, lengths, flags, rope_t, dst_k, dst_v,
+                   dst_pos, dst_frame, current_t, mode, rel_max, soft):
+    """refresh_readout_layout (scatter_copy.cu:77-168) on numpy arrays, in place."""
+    for s, (sk, sv, sp) in enumerate(zip(srcs_k, srcs_v, srcs_pos)):
+        n, off, fl = int(lengths[s]), int(offsets[s]), int(flags[s])
+        if n <= 0:
+            continue
+        dst_k[off:off + n] = sk[:n]
+        dst_v[off:off + n] = sv[:n]
+        for r in range(n):
+            t = int(sp[r, 0])
+            if fl & 4:
+                mt = int(rope_t[s])
+            elif fl & 1:
+                mt = legacy_map_t(t, current_t, mode, rel_max, soft)
+            else:
+                mt = t
+            dst_pos[off + r] = (mt, sp[r, 1], sp[r, 2])
+            dst_frame[off + r] = t if fl & 2 else mt
+
+
+def legacy_scatter_copy(srcs, lengths, offsets, dst):
+    """scatter_copy (scatter_copy.cu:13-47): rows of each source into dst, in place."""
+    for s, src in enumerate(srcs):
+        n, off = int(lengths[s]), int(offsets[s])
+        if n > 0:
+            dst[off:off + n] = src[:n]
+
+
+def legacy_write_frames(k_seq, v_seq, pos_seq, frame_desc, store_k, store_v, store_pos):
+    """anchor_store_write_frames (scatter_copy.cu:170-225): whole frames into slots."""
+    F = store_k.shape[1]
+    for src_frame, slot in np.asarray(frame_desc).reshape(-1, 2):
+        if src_frame < 0 or slot < 0:
+            continue
+        store_k[slot] = k_seq[src_frame * F:(src_frame + 1) * F]
+        store_v[slot] = v_seq[src_frame * F:(src_frame + 1) * F]
+        store_pos[slot] = pos_seq[src_frame * F:(src_frame + 1) * F]

@@ -120,7 +120,44 @@ def run_merge(c, dev, out, p):
     out[p + "tpg"] = mgr.merge_accum_tokens_per_group()[0].cpu().numpy()
 
 
-RUNNERS = {"state": run_state, "plan": run_plan, "pack": run_pack, "merge": run_merge}
+def run_legacy(c, dev, out, p):
+    """refresh_readout_layout, anchor_store_write_frames and scatter_copy of the
+    reference on the recorded sources (one call each)."""
+    n = int(c[p + "nseg"])
+    sk = [_bf(c[p + f"sk{s}"], dev) for s in range(n)]
+    sv = [_bf(c[p + f"sv{s}"], dev) for s in range(n)]
+    sp = [torch.from_numpy(c[p + f"sp{s}"]).to(dev) for s in range(n)]
+    t = lambda k: torch.from_numpy(c[p + k]).to(dev)  # noqa: E731
+    rows, D = int(c[p + "rows"]), int(c[p + "D"])
+    dk = torch.zeros(rows, D, dtype=torch.bfloat16, device=dev)
+    dv = torch.zeros_like(dk)
+    dp = torch.full((rows, 3), -7, dtype=torch.int64, device=dev)
+    df = torch.full((rows,), -7, dtype=torch.int64, device=dev)
+    ptr = lambda: torch.empty(n, dtype=torch.int64, device=dev)  # noqa: E731
+    torch.ops.adahead.refresh_readout_layout(
+        sk, sv, sp, ptr(), ptr(), ptr(), t("off"), t("len"), t("flags"), t("rope_t"), dk, dv, dp,
+        df, D, int(c[p + "cur"]), str(c[p + "mode"]), int(c[p + "relmax"]),
+        float(c[p + "soft"]))
+    out[p + "dk"], out[p + "dv"] = _u16(dk), _u16(dv)
+    out[p + "dp"], out[p + "df"] = dp.cpu().numpy(), df.cpu().numpy()
+    # anchor_store_write_frames
+    kq, vq = _bf(c[p + "kseq"], dev), _bf(c[p + "vseq"], dev)
+    pq = t("pseq")
+    cap, F = int(c[p + "cap"]), int(c[p + "F"])
+    stk = torch.zeros(cap, F, D, dtype=torch.bfloat16, device=dev)
+    stv = torch.zeros_like(stk)
+    stp = torch.zeros(cap, F, 3, dtype=torch.int64, device=dev)
+    torch.ops.adahead.anchor_store_write_frames(kq, vq, pq, t("fdesc"), stk, stv, stp)
+    out[p + "stk"], out[p + "stv"], out[p + "stp"] = _u16(stk), _u16(stv), stp.cpu().numpy()
+    # scatter_copy of the same sources into a flat workspace
+    ws = torch.zeros(rows, D, dtype=torch.bfloat16, device=dev)
+    ptrs = torch.tensor([x.data_ptr() for x in sk], dtype=torch.int64, device=dev)
+    torch.ops.adahead.scatter_copy(ptrs, t("len"), t("off"), ws, D)
+    out[p + "ws"] = _u16(ws)
+
+
+RUNNERS = {"state": run_state, "plan": run_plan, "pack": run_pack, "merge": run_merge,
+           "legacy": run_legacy}
 
 
 def main(inp: str, outp: str) -> None:

@@ -634,16 +634,148 @@ void unsupported_legacy(const char* name) {
   TORCH_CHECK(false, name, " belongs to the AdaptiveKVCache / CppStrategyManager path, which "
               "this library does not build; the MegaCache path does not call it");
 }
-void scatter_copy(Tensor, Tensor, Tensor, Tensor, int64_t) { unsupported_legacy("scatter_copy"); }
-void apply_pos_override(Tensor, Tensor, Tensor, Tensor) { unsupported_legacy("apply_pos_override"); }
-void anchor_store_write_frames(Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor) {
-  unsupported_legacy("anchor_store_write_frames");
+// ---- AdaptiveKVCache / CppStrategyManager ops (scatter_copy_bind.cpp:449-684) ----
+void check_i64_1d(const Tensor& t, const char* name, int64_t n, const Tensor& like) {
+  TORCH_CHECK(t.is_cuda() && t.dtype() == at::kLong && t.dim() == 1 && t.is_contiguous(),
+              name, " must be a contiguous 1-D int64 CUDA tensor");
+  TORCH_CHECK(t.size(0) >= n, name, " is too small");
+  TORCH_CHECK(t.device() == like.device(), name, ": device mismatch");
 }
-void refresh_readout_layout(std::vector<Tensor>, std::vector<Tensor>, std::vector<Tensor>,
-                            Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor,
-                            Tensor, Tensor, Tensor, int64_t, int64_t, std::string, int64_t,
-                            double) {
-  unsupported_legacy("refresh_readout_layout");
+
+void scatter_copy(Tensor src_ptrs, Tensor lengths, Tensor offsets, Tensor dst, int64_t col_dim) {
+  TORCH_CHECK(dst.is_cuda() && dst.is_contiguous(), "scatter_copy: dst must be contiguous CUDA");
+  const int64_t n = src_ptrs.size(0);
+  if (n == 0) return;
+  check_i64_1d(src_ptrs, "src_ptrs", n, dst);
+  check_i64_1d(lengths, "lengths", n, dst);
+  check_i64_1d(offsets, "offsets", n, dst);
+  c10::cuda::CUDAGuard g(dst.device());
+  check_rc(pkv_scatter_copy(src_ptrs.data_ptr<int64_t>(), lengths.data_ptr<int64_t>(),
+                            offsets.data_ptr<int64_t>(), dst.data_ptr(),
+                            col_dim * int64_t(dst.element_size()), int(n), stream_of(dst)),
+           "scatter_copy");
+}
+
+void apply_pos_override(Tensor pos, Tensor starts, Tensor ends, Tensor vals) {
+  TORCH_CHECK(pos.is_cuda() && pos.dtype() == at::kLong && pos.dim() == 2 && pos.size(1) == 3 &&
+                  pos.is_contiguous(),
+              "apply_pos_override: pos must be a contiguous [N, 3] int64 CUDA tensor");
+  const int64_t m = starts.size(0);
+  if (m == 0) return;
+  check_i64_1d(starts, "starts", m, pos);
+  check_i64_1d(ends, "ends", m, pos);
+  check_i64_1d(vals, "vals", m, pos);
+  c10::cuda::CUDAGuard g(pos.device());
+  check_rc(pkv_pos_override(pos.data_ptr<int64_t>(), starts.data_ptr<int64_t>(),
+                            ends.data_ptr<int64_t>(), vals.data_ptr<int64_t>(), int(m),
+                            stream_of(pos)),
+           "apply_pos_override");
+}
+
+// Host list of tensor addresses -> device int64 array, on the current stream.
+// The host copy is staged before cudaMemcpyAsync returns (pageable source).
+void copy_ptrs(const std::vector<Tensor>& ts, Tensor dst, const Tensor& like, const char* name) {
+  std::vector<int64_t> host;
+  host.reserve(ts.size());
+  for (size_t i = 0; i < ts.size(); ++i) {
+    TORCH_CHECK(ts[i].is_cuda() && ts[i].is_contiguous(), name, "[", i,
+                "] must be a contiguous CUDA tensor");
+    TORCH_CHECK(ts[i].device() == like.device(), name, "[", i, "] is on another device");
+    host.push_back(reinterpret_cast<int64_t>(ts[i].data_ptr()));
+  }
+  if (host.empty()) return;
+  C10_CUDA_CHECK(cudaMemcpyAsync(dst.data_ptr<int64_t>(), host.data(),
+                                 host.size() * sizeof(int64_t), cudaMemcpyHostToDevice,
+                                 static_cast<cudaStream_t>(stream_of(dst))));
+}
+
+int mapping_mode_code(const std::string& mode) {
+  if (mode == "relative_clamp") return 1;
+  if (mode == "relative_softcap") return 2;
+  return 0;  // "none" and anything else (scatter_copy_bind.cpp:484-489)
+}
+
+void refresh_readout_layout(std::vector<Tensor> src_k, std::vector<Tensor> src_v,
+                            std::vector<Tensor> src_pos, Tensor src_ptrs_k, Tensor src_ptrs_v,
+                            Tensor src_ptrs_pos, Tensor offsets, Tensor lengths, Tensor flags,
+                            Tensor dynamic_rope_t, Tensor dst_k_raw, Tensor dst_v,
+                            Tensor dst_rope_pos, Tensor dst_frame_ids, int64_t head_dim,
+                            int64_t current_t, std::string mode, int64_t rel_max,
+                            double soft_factor) {
+  const int64_t n = int64_t(src_k.size());
+  TORCH_CHECK(src_v.size() == src_k.size() && src_pos.size() == src_k.size(),
+              "refresh_readout_layout: src_k / src_v / src_pos lengths differ");
+  if (n == 0) return;
+  for (const Tensor* t : {&dst_k_raw, &dst_v, &dst_rope_pos, &dst_frame_ids})
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->device() == dst_k_raw.device(),
+                "refresh_readout_layout: destinations must be contiguous on one CUDA device");
+  TORCH_CHECK(dst_rope_pos.dtype() == at::kLong && dst_frame_ids.dtype() == at::kLong,
+              "refresh_readout_layout: dst_rope_pos / dst_frame_ids must be int64");
+  TORCH_CHECK(dst_k_raw.dtype() == dst_v.dtype(), "refresh_readout_layout: dst dtype mismatch");
+  TORCH_CHECK(dst_k_raw.size(1) == head_dim && dst_v.size(1) == head_dim,
+              "refresh_readout_layout: head_dim mismatch");
+  TORCH_CHECK(dst_rope_pos.size(1) == 3, "refresh_readout_layout: dst_rope_pos must be [N, 3]");
+  for (const auto& pr : {std::make_pair(&src_ptrs_k, "src_ptrs_k"),
+                         std::make_pair(&src_ptrs_v, "src_ptrs_v"),
+                         std::make_pair(&src_ptrs_pos, "src_ptrs_pos"),
+                         std::make_pair(&offsets, "offsets"), std::make_pair(&lengths, "lengths"),
+                         std::make_pair(&flags, "flags"),
+                         std::make_pair(&dynamic_rope_t, "dynamic_rope_t")})
+    check_i64_1d(*pr.first, pr.second, n, dst_k_raw);
+  for (int64_t i = 0; i < n; ++i) {
+    TORCH_CHECK(src_k[i].dtype() == dst_k_raw.dtype() && src_v[i].dtype() == dst_v.dtype(),
+                "refresh_readout_layout: source dtype mismatch");
+    TORCH_CHECK(src_pos[i].dtype() == at::kLong && src_pos[i].size(1) == 3,
+                "refresh_readout_layout: src_pos must be [rows, 3] int64");
+    TORCH_CHECK(src_k[i].size(1) == head_dim && src_v[i].size(1) == head_dim,
+                "refresh_readout_layout: source head_dim mismatch");
+  }
+  c10::cuda::CUDAGuard g(dst_k_raw.device());
+  copy_ptrs(src_k, src_ptrs_k, dst_k_raw, "src_k");
+  copy_ptrs(src_v, src_ptrs_v, dst_k_raw, "src_v");
+  copy_ptrs(src_pos, src_ptrs_pos, dst_k_raw, "src_pos");
+  check_rc(pkv_refresh_readout_layout(
+               src_ptrs_k.data_ptr<int64_t>(), src_ptrs_v.data_ptr<int64_t>(),
+               src_ptrs_pos.data_ptr<int64_t>(), offsets.data_ptr<int64_t>(),
+               lengths.data_ptr<int64_t>(), flags.data_ptr<int64_t>(),
+               dynamic_rope_t.data_ptr<int64_t>(), dst_k_raw.data_ptr(), dst_v.data_ptr(),
+               dst_rope_pos.data_ptr<int64_t>(), dst_frame_ids.data_ptr<int64_t>(),
+               head_dim * int64_t(dst_k_raw.element_size()), current_t, mapping_mode_code(mode),
+               rel_max, float(soft_factor), int(n), stream_of(dst_k_raw)),
+           "refresh_readout_layout");
+}
+
+void anchor_store_write_frames(Tensor k_seq, Tensor v_seq, Tensor pos_seq, Tensor frame_desc,
+                               Tensor store_k, Tensor store_v, Tensor store_pos) {
+  for (const Tensor* t : {&k_seq, &v_seq, &pos_seq, &frame_desc, &store_k, &store_v, &store_pos})
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->device() == store_k.device(),
+                "anchor_store_write_frames: tensors must be contiguous on one CUDA device");
+  TORCH_CHECK(k_seq.dtype() == store_k.dtype() && v_seq.dtype() == store_v.dtype(),
+              "anchor_store_write_frames: K/V dtype mismatch");
+  TORCH_CHECK(pos_seq.dtype() == at::kLong && store_pos.dtype() == at::kLong &&
+                  frame_desc.dtype() == at::kLong,
+              "anchor_store_write_frames: pos / frame_desc must be int64");
+  TORCH_CHECK(k_seq.dim() == 2 && v_seq.dim() == 2 && pos_seq.dim() == 2 && pos_seq.size(1) == 3,
+              "anchor_store_write_frames: k_seq / v_seq [tokens, D], pos_seq [tokens, 3]");
+  TORCH_CHECK(frame_desc.dim() == 2 && frame_desc.size(1) == 2,
+              "anchor_store_write_frames: frame_desc must be [N, 2]");
+  TORCH_CHECK(store_k.dim() == 3 && store_v.dim() == 3 && store_pos.dim() == 3 &&
+                  store_pos.size(2) == 3,
+              "anchor_store_write_frames: stores must be [capacity, frame_seqlen, D / 3]");
+  TORCH_CHECK(store_k.size(1) == store_v.size(1) && store_k.size(2) == store_v.size(2) &&
+                  store_pos.size(1) == store_k.size(1),
+              "anchor_store_write_frames: store shapes disagree");
+  TORCH_CHECK(k_seq.size(1) == store_k.size(2) && v_seq.size(1) == store_v.size(2),
+              "anchor_store_write_frames: head_dim mismatch");
+  const int64_t n = frame_desc.size(0);
+  if (n == 0) return;
+  c10::cuda::CUDAGuard g(store_k.device());
+  check_rc(pkv_anchor_store_write_frames(
+               k_seq.data_ptr(), v_seq.data_ptr(), pos_seq.data_ptr<int64_t>(),
+               frame_desc.data_ptr<int64_t>(), store_k.data_ptr(), store_v.data_ptr(),
+               store_pos.data_ptr<int64_t>(), store_k.size(1),
+               store_k.size(2) * int64_t(store_k.element_size()), int(n), stream_of(store_k)),
+           "anchor_store_write_frames");
 }
 std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> pyramidkv_plan(Mgr, int64_t, int64_t) {
   unsupported_legacy("pyramidkv_plan");
