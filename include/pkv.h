@@ -339,6 +339,16 @@ int pkv_anchor_store_write_frames(const void *k_seq, const void *v_seq, const in
                                   int num_frames, pkv_stream_t stream);
 
 /*
+ * Self-test of the kernels' bounded waits: one GPU thread waits, with the
+ * attention kernel's wait helper, on a barrier that nothing completes, for
+ * limit_ns (<= 4 s) nanoseconds; the wait then gives up, ORs PKV_ST_TIMEOUT
+ * into *status and writes 0 to *result (1 would mean the wait completed).
+ * No counterpart in the reference; it exercises the timeout path on the GPU
+ * without a fault or a hang.
+ */
+int pkv_wait_selftest(int32_t *status, int64_t limit_ns, int32_t *result, pkv_stream_t stream);
+
+/*
  * Evaluation order of the RoPE pair rotation in the pack kernel: 0 =
  * fma(kr, fr, -(ki*fi)) / fma(kr, fi, ki*fr) (default), 1 = fma on the second
  * product, 2 = no contraction.  Returns the previous order.  No counterpart in

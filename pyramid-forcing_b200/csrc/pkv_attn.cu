@@ -74,12 +74,12 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
 // Bounded wait: false when the CTA is aborting (limit reached here or in
 // another role).
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
-                                          int32_t* status) {
+                                          int32_t* status, uint64_t limit_ns = kTimeoutNs) {
   if (mbar_try(b, parity)) return true;
   const uint64_t t0 = now_ns();
   while (!mbar_try(b, parity)) {
     if (*abort) return false;
-    if (now_ns() - t0 > kTimeoutNs) {
+    if (now_ns() - t0 > limit_ns) {
       *abort = 1;
       flag(status, PKV_ST_TIMEOUT);
       return false;
@@ -698,6 +698,21 @@ __global__ void __launch_bounds__(kSimtRows)
   for (int d = 0; d < D; ++d) orow[d] = static_cast<uint16_t>(f32_to_bf16_bits(acc[d] * inv));
 }
 
+// Self-test of the bounded wait: one thread waits on an mbarrier that nothing
+// arrives at, with the attention kernel's wait helper and a caller-chosen
+// limit, so the timeout path (status bit, return) runs on the GPU without a
+// fault or a hang.
+__global__ void wait_selftest_kernel(int32_t* status, uint64_t limit_ns, int32_t* result) {
+  __shared__ uint64_t bar;
+  __shared__ int abort;
+  if (threadIdx.x != 0) return;
+  abort = 0;
+  mbar_init(&bar, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const bool ok = mbar_wait(&bar, 0, &abort, status, limit_ns);
+  *result = ok ? 1 : 0;
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -796,4 +811,12 @@ extern "C" int pkv_attention(const uint16_t* q, int64_t q_row_stride, int64_t q_
   return launch_attention(q, q_row_stride, q_head_stride, k, v, kv_rows, cu_seqlens_k,
                           num_chunks, num_heads, rows_per_chunk, head_dim, softmax_scale, out,
                           o_row_stride, o_head_stride, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pkv_wait_selftest(int32_t* status, int64_t limit_ns, int32_t* result,
+                                 pkv_stream_t stream) {
+  if (!status || !result || limit_ns <= 0 || limit_ns > int64_t(kTimeoutNs)) return PKV_EINVAL;
+  pkv::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, uint64_t(limit_ns), result);
+  return pkv::launch_status();
 }
