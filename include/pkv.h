@@ -297,6 +297,22 @@ int pkv_attend_noalloc(const pkv_cache_t *cache, const uint8_t *states_layer, in
                        uint16_t *out, int64_t o_tok_stride, int64_t o_head_stride,
                        int64_t *token_counter, pkv_stream_t stream);
 
+/*
+ * 3D RoPE of a query block (model side, before pkv_attend): token s of the
+ * frames x grid_h x grid_w grid, head h, pair p of head_dim is multiplied in
+ * complex float64 by freqs_t[start_frame + f] (p < t_cols), freqs_y[row]
+ * (next y_cols pairs) or freqs_x[col] (the rest), then rounded to float32 and
+ * to bf16 (torch's float64 -> bf16 cast); tokens past the grid are copied.  Tables: float64 [rows, cols, 2] (re, im).
+ * x / out: bf16 at base + tok * tok_stride + h * head_stride (16-byte aligned,
+ * strides multiples of 8 elements).
+ * Replaces: causal_rope_apply (wan/modules/causal_model.py:30-63) for one sample.
+ */
+int pkv_rope_q(const uint16_t *x, int64_t x_tok_stride, int64_t x_head_stride, uint16_t *out,
+               int64_t o_tok_stride, int64_t o_head_stride, int64_t tokens, int heads,
+               int head_dim, int64_t start_frame, int frames, int grid_h, int grid_w,
+               const double *freqs_t, int t_rows, int t_cols, const double *freqs_y, int y_rows,
+               int y_cols, const double *freqs_x, int x_rows, int x_cols, pkv_stream_t stream);
+
 /* ---- AdaptiveKVCache / CppStrategyManager ops (not on the MegaCache path) ----
  * Same bytes as the reference's kernels; launched on `stream` (the
  * reference's use the legacy default stream).  One CTA per segment / frame.

@@ -525,3 +525,32 @@ def legacy_write_frames(k_seq, v_seq, pos_seq, frame_desc, store_k, store_v, sto
         store_k[slot] = k_seq[src_frame * F:(src_frame + 1) * F]
         store_v[slot] = v_seq[src_frame * F:(src_frame + 1) * F]
         store_pos[slot] = pos_seq[src_frame * F:(src_frame + 1) * F]
+
+
+# ---------------------------------------------------------------------------
+# Query RoPE (wan/modules/causal_model.py:30-63)
+# ---------------------------------------------------------------------------
+def rope_q(x_bf16: np.ndarray, freqs_full, start_frame: int, F: int, Hg: int, Wg: int):
+    """One sample: x uint16 [L, n, D] -> rotated uint16 [L, n, D] (complex128
+    products a*c - b*d, a*d + b*c, rounded to float32 then bf16; tokens past
+    F*Hg*Wg copied).  wan/modules/causal_model.py:30-63."""
+    import torch
+    L, n, D = x_bf16.shape
+    c = D // 2
+    z = freqs_full.detach().cpu().numpy() if isinstance(freqs_full, torch.Tensor) else freqs_full
+    parts = np.split(z, [c - 2 * (c // 3), c - (c // 3)], axis=1)
+    S = F * Hg * Wg
+    f_idx = np.arange(S) // (Hg * Wg)
+    h_idx = (np.arange(S) // Wg) % Hg
+    w_idx = np.arange(S) % Wg
+    fr = np.concatenate([parts[0][start_frame + f_idx], parts[1][h_idx], parts[2][w_idx]], axis=1)
+    xf = bf16_to_f32(x_bf16[:S]).astype(np.float64).reshape(S, n, c, 2)
+    a, b = xf[..., 0], xf[..., 1]
+    cr, ci = fr.real[:, None, :], fr.imag[:, None, :]
+    re = a * cr - b * ci
+    im = a * ci + b * cr
+    out = x_bf16.copy()
+    # torch casts float64 -> bf16 through float32 (two roundings), as the
+    # reference's .type_as(x) does
+    out[:S] = f32_to_bf16(np.stack([re, im], -1).reshape(S, n, D).astype(np.float32))
+    return out

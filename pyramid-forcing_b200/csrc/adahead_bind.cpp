@@ -627,6 +627,31 @@ Tensor op_attention(Tensor q, Tensor k, Tensor v, Tensor cu, int64_t num_chunks,
   return out;
 }
 
+// 3D RoPE of a query block of one sample: x [tokens, H, D] bf16 (last dim
+// contiguous), tables float64 [rows, cols * 2] (re, im) for the t / y / x
+// parts; returns a new [tokens, H, D] tensor (causal_model.py:30-63).
+Tensor op_rope_q(Tensor x, Tensor ft, Tensor fy, Tensor fx, int64_t start_frame, int64_t frames,
+                 int64_t grid_h, int64_t grid_w) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 3,
+              "pkv_rope_q: x must be a [tokens, H, D] bf16 CUDA tensor");
+  for (const Tensor* t : {&ft, &fy, &fx})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kDouble && t->dim() == 2 &&
+                    t->is_contiguous() && t->size(1) % 2 == 0 && t->device() == x.device(),
+                "pkv_rope_q: tables must be contiguous [rows, cols * 2] float64 on x's device");
+  const c10::cuda::CUDAGuard g(x.device());
+  auto xx = x.stride(2) == 1 ? x : x.contiguous();
+  auto out = at::empty(x.sizes(), x.options());
+  check_rc(pkv_rope_q(reinterpret_cast<const uint16_t*>(xx.data_ptr()), xx.stride(0),
+                      xx.stride(1), reinterpret_cast<uint16_t*>(out.data_ptr()), out.stride(0),
+                      out.stride(1), x.size(0), int(x.size(1)), int(x.size(2)), start_frame,
+                      int(frames), int(grid_h), int(grid_w), ft.data_ptr<double>(),
+                      int(ft.size(0)), int(ft.size(1) / 2), fy.data_ptr<double>(),
+                      int(fy.size(0)), int(fy.size(1) / 2), fx.data_ptr<double>(),
+                      int(fx.size(0)), int(fx.size(1) / 2), stream_of(xx)),
+           "pkv_rope_q");
+  return out;
+}
+
 int64_t op_status(Mgr mgr) { return take_status(mgr); }
 int64_t op_rope_rounding(int64_t mode) { return pkv_set_rope_rounding(int(mode)); }
 
@@ -923,6 +948,8 @@ TORCH_LIBRARY(adahead, m) {
         "int rows_per_chunk, float softmax_scale) -> Tensor");
   m.def("pkv_status(__torch__.torch.classes.adahead.PyramidKVCacheManager mgr) -> int");
   m.def("pkv_rope_rounding(int mode) -> int");
+  m.def("pkv_rope_q(Tensor x, Tensor ft, Tensor fy, Tensor fx, int start_frame, int frames, "
+        "int grid_h, int grid_w) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(adahead, CUDA, m) {
@@ -936,6 +963,7 @@ TORCH_LIBRARY_IMPL(adahead, CUDA, m) {
   m.impl("mega_merge_accum", mega_merge_accum);
   m.impl("pkv_cache_update", op_cache_update);
   m.impl("pkv_attend", op_attend);
+  m.impl("pkv_rope_q", op_rope_q);
   m.impl("pkv_attend_pack", op_attend_pack);
   m.impl("pkv_attend_attention", op_attend_attention);
   m.impl("pkv_attention", op_attention);
