@@ -1,0 +1,98 @@
+"""Head-parallel cache path on 2 GPUs (NCCL), against one GPU.
+
+Two spawned ranks (one per GPU) each own 2 of the 4 heads of a small model
+and feed ``HeadParallelMegaCache`` their token shard of every block; rank 0
+also runs the single-GPU MegaCache over all heads on the same inputs.  The
+gathered outputs of the ranks must equal the single-GPU outputs bit for bit.
+Skipped with fewer than 2 GPUs.  NVLS is off (NCCL_NVLS_ENABLE=0) and the
+process group has a short timeout, so a failing rank ends the test with an
+error instead of a wait.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import pkv_oracle as O
+
+pytestmark = pytest.mark.gpu
+WORLD = 2
+L, H, D, W, HG, F = 2, 4, 128, 13, 8, 3
+FSEQ = W * HG
+BLOCKS = 4
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _labels():
+    return np.array([[-1, 1, 2, 2], [2, 1, -1, 1]])
+
+
+def _build(num_heads, labels, device, builder=None):
+    from pyramidkv import _mega_cache, policy
+    _, full = O.rope_freq_tables(D)
+    kw = dict(device=device, sink_time_mapping_mode="window_clamp", sink_time_clamp_min=18,
+              sink_time_clamp_max=21, spatial_width=W, spatial_height=HG, freqs=full)
+    comps = policy.compositions_from_labels(labels)
+    if builder is None:
+        return _mega_cache.build_mega_caches(L, num_heads, D, FSEQ, 3, 24, 4, comps, **kw)
+    return builder(L, H, D, FSEQ, 3, 24, 4, comps, **kw)
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(21)
+    mk = lambda: torch.randn(1, F * FSEQ, H, D, generator=g).to(torch.bfloat16)  # noqa: E731
+    return [[(mk(), mk(), mk()) for _ in range(L)] for _ in range(BLOCKS)]
+
+
+def _worker(rank: int, port: int, out_dir: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = f"cuda:{rank}"
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from pyramidkv import head_parallel as hp
+        caches = _build(H, _labels(), dev, builder=hp.build_head_parallel_caches)
+        t0, t1 = hp.token_range(rank, WORLD, F * FSEQ)
+        got = []
+        for blk, layers in enumerate(_inputs()):
+            start = blk * F * FSEQ
+            for mode in ("noisy", "clean"):
+                for layer, (k, v, q) in enumerate(layers):
+                    sh = lambda x: x[:, t0:t1].contiguous().to(dev)  # noqa: E731
+                    caches[layer].update(sh(k), sh(v), start, cache_update_mode=mode)
+                    got.append(caches[layer].attend(sh(q), start).cpu())
+        torch.cuda.synchronize()
+        torch.save(got, os.path.join(out_dir, f"rank{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_head_parallel_two_gpus_matches_one_gpu(tmp_path):
+    mp.spawn(_worker, args=(_port(), str(tmp_path)), nprocs=WORLD, join=True)
+    ref = _build(H, _labels(), "cuda:0")
+    want = []
+    for blk, layers in enumerate(_inputs()):
+        start = blk * F * FSEQ
+        for mode in ("noisy", "clean"):
+            for layer, (k, v, q) in enumerate(layers):
+                ref[layer].update(k.cuda(), v.cuda(), start, cache_update_mode=mode)
+                want.append(ref[layer].attend(q.cuda(), start).cpu())
+    parts = [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) for r in range(WORLD)]
+    for i, w in enumerate(want):
+        got = torch.cat([parts[r][i] for r in range(WORLD)], dim=1)
+        assert torch.equal(got.view(torch.int16), w.view(torch.int16)), i
