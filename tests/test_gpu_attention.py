@@ -74,6 +74,30 @@ def test_attention_rescale_path_and_empty_segment(cuda):
     assert out[:, 1].abs().max().item() == 0.0
 
 
+@pytest.mark.parametrize("seed", [0, 1])
+def test_attention_max_jumps_between_tiles(cuda, seed):
+    """Keys whose magnitude jumps from one 128-key tile to the next: a row
+    maximum moving by 2^8..2^64 (log2 units) while P is formed from the old
+    reference, by more than 2^64 (P redone from S), on the last full tile before a
+    partial one, and on the last tile of a segment.  Query rows span two full
+    tiles and a 24-row tail."""
+    from pyramidkv import _ops
+    C, H, Lq, D = 1, 4, 280, 128
+    pattern = [[1, 6, 6, 40, 40, 1], [1, 1, 1, 6], [1, 1, 1, 1, 6, 6], [1, 1, 40]]
+    tails = [7, 0, 100, 0]
+    lens = [128 * (len(p_) - (1 if t else 0)) + t for p_, t in zip(pattern, tails)]
+    q, k, v, cu = _case(cuda, C, H, Lq, D, lens, seed=seed)
+    kf = k.float()
+    cuh = cu.cpu()
+    for i, pat in enumerate(pattern):
+        a = int(cuh[i])
+        for tile, f in enumerate(pat):
+            kf[a + 128 * tile:min(a + 128 * (tile + 1), int(cuh[i + 1]))] *= f
+    k = kf.to(torch.bfloat16)
+    out = _ops.ops().pkv_attention(q, k, v, cu, C, Lq, 0.088)
+    _check(out, _reference(q, k, v, cu, C, H, Lq, 0.088))
+
+
 def test_attention_strided_q_layout(cuda):
     """Q as a non-contiguous view ([1, L_q, H, D] sliced from a wider tensor)."""
     from pyramidkv import _ops
