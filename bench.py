@@ -56,7 +56,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--kernel-case", choices=["attn", "pack"], default=None,
+    ap.add_argument("--kernel-case", choices=["attn", "pack", "update"], default=None,
                     help="run one kernel on a standalone steady-state-sized input "
                          "(small device footprint, for profiler captures) and exit")
     ap.add_argument("--kernel-iters", type=int, default=4)
@@ -503,6 +503,30 @@ def run_kernel_case(args):
         cud = cu.to(dev)
         run = lambda: ops.pkv_attention(q[0], k, v, cud, C, FSEQ, D_ ** -0.5)  # noqa: E731
         work, unit = 4.0 * FSEQ * D_ * T, "FLOP"
+    elif args.kernel_case == "update":
+        # one layer with a third of its heads merge heads, after 30 blocks; a
+        # run is the noisy and the clean update of the next block (route, copy
+        # and, on the clean pass, merge kernels)
+        from pyramidkv import _mega_cache
+        labels = policy.random_labels(1, H_, seed=args.seed, merge_fraction=1.0 / 3.0)
+        caches = _mega_cache.build_mega_caches(
+            1, H_, D_, FSEQ, 3, 24, 4, policy.compositions_from_labels(labels),
+            device="cuda:0", sink_time_mapping_mode="window_clamp", sink_time_clamp_min=18,
+            sink_time_clamp_max=21, spatial_width=W_, spatial_height=HG_, freqs=rope_table(D_))
+        c = caches[0]
+        shape = (1, C * FSEQ, H_, D_)
+        kk = torch.randn(shape, generator=g).to(dev, torch.bfloat16)
+        vv = torch.randn(shape, generator=g).to(dev, torch.bfloat16)
+        for blk in range(30):
+            c.update(kk, vv, blk * C * FSEQ, cache_update_mode="clean")
+        nxt = [30]
+
+        def run():
+            start = nxt[0] * C * FSEQ
+            nxt[0] += 1
+            c.update(kk, vv, start, cache_update_mode="noisy")
+            c.update(kk, vv, start, cache_update_mode="clean")
+        work, unit = 2 * 2 * 2 * kk.numel() * 2, "B"   # K and V of 2 passes, read + written
     else:
         from pyramidkv import _mega_cache
         labels = policy.random_labels(1, H_, seed=args.seed)
