@@ -471,15 +471,16 @@ __global__ void __launch_bounds__(kThreads2, 1)
         // 128x128x16 MMAs (64 cycles each) only if little scalar work sits
         // between them: measured on B200, issue takes 64 cycles per MMA with
         // precomputed descriptors and 110-260 with per-MMA address arithmetic.
-        constexpr uint32_t d_hi = (1024u >> 4) | (1u << 14) | (2u << 29);
-        const uint32_t q_lo0 = (su32(sm.q[0]) >> 4) | (1u << 16);
-        const uint32_t q_lo1 = (su32(sm.q[1]) >> 4) | (1u << 16);
-        const uint32_t k_lo0 = (su32(sm.k[0]) >> 4) | (1u << 16);
-        const uint32_t k_lo1 = (su32(sm.k[1]) >> 4) | (1u << 16);
-        const uint32_t v_lo0 = (su32(sm.v[0]) >> 4) | ((kHalfBytes >> 4) << 16);
-        const uint32_t v_lo1 = (su32(sm.v[1]) >> 4) | ((kHalfBytes >> 4) << 16);
+        const uint64_t dq0 = sdesc_sw128(su32(sm.q[0]), 16, 1024);
+        const uint32_t d_hi = uint32_t(dq0 >> 32);  // SBO and layout bits, the same for all
+        const uint32_t q_lo0 = uint32_t(dq0);
+        const uint32_t q_lo1 = uint32_t(sdesc_sw128(su32(sm.q[1]), 16, 1024));
+        const uint32_t k_lo0 = uint32_t(sdesc_sw128(su32(sm.k[0]), 16, 1024));
+        const uint32_t k_lo1 = uint32_t(sdesc_sw128(su32(sm.k[1]), 16, 1024));
+        const uint32_t v_lo0 = uint32_t(sdesc_sw128(su32(sm.v[0]), kHalfBytes, 1024));
+        const uint32_t v_lo1 = uint32_t(sdesc_sw128(su32(sm.v[1]), kHalfBytes, 1024));
         static_assert(kStages2 == 2, "descriptor words are kept for two stages");
-        auto desc = [](uint32_t lo) { return (uint64_t(d_hi) << 32) | lo; };
+        auto desc = [d_hi](uint32_t lo) { return (uint64_t(d_hi) << 32) | lo; };
         auto issue_qk = [&](int t, int j) {
           const uint32_t q_lo = t ? q_lo1 : q_lo0;
           const uint32_t k_lo = (j & 1) ? k_lo1 : k_lo0;
