@@ -191,6 +191,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch m) {
     const int ng = cache[a].num_groups;
     const uint16_t* kbase = m.new_k + int64_t(f) * m.frame_stride + int64_t(h) * m.head_stride;
     const uint16_t* vbase = m.new_v + int64_t(f) * m.frame_stride + int64_t(h) * m.head_stride;
+    // head_dim 128 with 8-byte aligned rows: lane owns dims 4*lane..4*lane+3,
+    // and a group's token rows are loaded 8 at a time before they are added
+    // in list order (the adds stay sequential per element, as the reference's)
+    const bool vec4 = D == 128 && (m.tok_stride & 3) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(kbase) | reinterpret_cast<uintptr_t>(vbase)) & 7) == 0;
     for (int gl = warp; gl < kGroupsPerCta; gl += kMergeThreads / 32) {
       const int g = g0 + gl;
       if (g >= MTPA) break;
@@ -200,6 +205,55 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch m) {
       const float divisor = tpg[gl];
       const float inv = divisor > 0.0f ? __frcp_rn(divisor) : 0.0f;
       const int64_t prow = (int64_t(h) * m.MMB + fin) * MTPA + g;
+      if (vec4) {
+        const int d0 = lane * 4;
+        float sk[4], sv[4];
+        if (fresh) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sk[e] = sv[e] = 0.0f;
+        } else {
+          const float4 k4 = *reinterpret_cast<const float4*>(ak + d0);
+          const float4 v4 = *reinterpret_cast<const float4*>(av + d0);
+          sk[0] = k4.x; sk[1] = k4.y; sk[2] = k4.z; sk[3] = k4.w;
+          sv[0] = v4.x; sv[1] = v4.y; sv[2] = v4.z; sv[3] = v4.w;
+        }
+        for (int i0 = lo; i0 < hi; i0 += 8) {
+          uint2 kr[8], vr[8];
+#pragma unroll
+          for (int b = 0; b < 8; ++b) {
+            if (i0 + b < hi) {
+              const int64_t t = list[i0 + b];
+              kr[b] = *reinterpret_cast<const uint2*>(kbase + t * m.tok_stride + d0);
+              vr[b] = *reinterpret_cast<const uint2*>(vbase + t * m.tok_stride + d0);
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < 8; ++b) {
+            if (i0 + b < hi) {
+              const uint32_t kw[2] = {kr[b].x, kr[b].y}, vw[2] = {vr[b].x, vr[b].y};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t kb = (e & 1) ? (kw[e >> 1] >> 16) : (kw[e >> 1] & 0xffffu);
+                const uint32_t vb = (e & 1) ? (vw[e >> 1] >> 16) : (vw[e >> 1] & 0xffffu);
+                sk[e] = __fadd_rn(sk[e], bf16_bits_to_f32(kb));
+                sv[e] = __fadd_rn(sv[e], bf16_bits_to_f32(vb));
+              }
+            }
+          }
+        }
+        *reinterpret_cast<float4*>(ak + d0) = make_float4(sk[0], sk[1], sk[2], sk[3]);
+        *reinterpret_cast<float4*>(av + d0) = make_float4(sv[0], sv[1], sv[2], sv[3]);
+        if (fin >= 0 && g < ng) {
+          uint2 ok, ov;
+          ok.x = f32_to_bf16_bits(__fmul_rn(sk[0], inv)) | (f32_to_bf16_bits(__fmul_rn(sk[1], inv)) << 16);
+          ok.y = f32_to_bf16_bits(__fmul_rn(sk[2], inv)) | (f32_to_bf16_bits(__fmul_rn(sk[3], inv)) << 16);
+          ov.x = f32_to_bf16_bits(__fmul_rn(sv[0], inv)) | (f32_to_bf16_bits(__fmul_rn(sv[1], inv)) << 16);
+          ov.y = f32_to_bf16_bits(__fmul_rn(sv[2], inv)) | (f32_to_bf16_bits(__fmul_rn(sv[3], inv)) << 16);
+          *reinterpret_cast<uint2*>(m.mk + prow * D + d0) = ok;
+          *reinterpret_cast<uint2*>(m.mv + prow * D + d0) = ov;
+        }
+        continue;
+      }
       for (int d = lane; d < D; d += 32) {
         float sk = fresh ? 0.0f : ak[d];
         float sv = fresh ? 0.0f : av[d];
