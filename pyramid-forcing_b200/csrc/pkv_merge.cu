@@ -15,7 +15,9 @@
 // 1560 tokens serially.  Here a CTA owns (head, tile of 32 groups): it builds
 // the token list of each of its groups in ascending token order (one warp,
 // match/ballot ranking), then every warp reduces whole groups with its lanes
-// spread over head_dim.  Each accumulator element still receives its tokens
+// spread over head_dim (for head_dim 128, 4 dims per lane, a group's token rows
+// loaded 8 at a time before they are added).  Each accumulator element still
+// receives its tokens
 // in ascending order, frame after frame, so the fp32 sums are bit-identical
 // to the reference's sequential loop.  The finalize multiplies by the
 // correctly rounded reciprocal (__frcp_rn), which equals the reference's
