@@ -17,9 +17,8 @@
 // match/ballot ranking), then every warp reduces whole groups with its lanes
 // spread over head_dim (for head_dim 128, 4 dims per lane, a group's token rows
 // loaded 8 at a time before they are added).  Each accumulator element still
-// receives its tokens
-// in ascending order, frame after frame, so the fp32 sums are bit-identical
-// to the reference's sequential loop.  The finalize multiplies by the
+// receives its tokens in ascending order, frame after frame, so the fp32 sums
+// are bit-identical to the reference's sequential loop.  The finalize multiplies by the
 // correctly rounded reciprocal (__frcp_rn), which equals the reference's
 // fast-math reciprocal for the power-of-two divisors these grids produce.
 #include "pkv_common.cuh"
