@@ -314,6 +314,7 @@ def cpu_sample(args, budget_s: float = 12.0, warm_blocks: int = 12):
     from oracle import pkv_oracle as O
     from pyramidkv import policy
 
+    O.set_threads(os.cpu_count() or 1)    # the pack over all host cores
     labels = policy.random_labels(L_, H_, seed=args.seed, merge_fraction=args.merge_fraction)
     states, caps = policy.states_from_labels(labels[:1], "baseline")
     tables, _ = O.rope_freq_tables(D_)
@@ -361,7 +362,8 @@ def cpu_baseline_json(fps, detail, cores):
                        f"({detail['kv_tokens']} packed K/V tokens): noisy+clean update, plan+pack "
                        f"with RoPE, fp32 attention of {detail['segments_timed']}/"
                        f"{detail['segments']} (chunk, head) segments scaled to all; "
-                       "C restatement single-threaded, attention numpy BLAS on all cores; "
+                       "C restatement (pack OpenMP over segments) and numpy BLAS attention "
+                       "on all cores; "
                        "scaled to 6000 layer-steps per 120-frame video"),
             "us_per_layer_step": detail["us_per_layer_step"]}
 

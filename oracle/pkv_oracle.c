@@ -37,6 +37,7 @@
 #include <stddef.h>
 #include <stdint.h>
 #include <stdlib.h>
+#include <pthread.h>
 #include <string.h>
 
 /* ---- bounds (anchor_store.cuh:39-45,148) ------------------------------- */
@@ -505,24 +506,44 @@ static inline void rot(float kr, float ki, float fr, float fi, int mode, float *
     }
 }
 
-/* pools as in orc_update_frames plus merge pools [L*H*MMB, MTPA, D].
- * k_out/v_out: [T, D]; pos_out: [T, 3] or NULL.  Tables: [rows, cols*2] fp32
- * or NULL (a NULL remap or all-NULL tables disables RoPE, as in the kernel). */
-void orc_pack(const uint16_t *sink_k, const uint16_t *sink_v, const uint16_t *mid_k,
-              const uint16_t *mid_v, const uint16_t *rec_k, const uint16_t *rec_v,
-              const uint16_t *mg_k, const uint16_t *mg_v, const int64_t *sink_pos,
-              const int64_t *mid_pos, const int64_t *rec_pos, const int64_t *mg_pos,
-              uint16_t *k_out, uint16_t *v_out, int64_t *pos_out, const int32_t *sk,
-              const int32_t *sg, const int32_t *sl, const int32_t *dst, int nseg,
-              const int64_t *tremap, const float *ft, int ft_rows, int ft_cols,
-              const float *fy, int fy_rows, int fy_cols, const float *fx, int fx_rows,
-              int fx_cols, int FSEQ, int MTPA, int D, int rope_mode) {
+/* Threads for orc_pack: segments are handed out from a shared counter, each
+ * writing its own output range.  1 by default, so the tests start no thread;
+ * the timed CPU baseline sets it to the host's core count. */
+static int g_threads = 1;
+void orc_set_threads(int n) { g_threads = n < 1 ? 1 : (n > 256 ? 256 : n); }
+
+typedef struct {
+    const uint16_t *sink_k, *sink_v, *mid_k, *mid_v, *rec_k, *rec_v, *mg_k, *mg_v;
+    const int64_t *sink_pos, *mid_pos, *rec_pos, *mg_pos;
+    uint16_t *k_out, *v_out;
+    int64_t *pos_out;
+    const int32_t *sk, *sg, *sl, *dst;
+    int nseg;
+    const int64_t *tremap;
+    const float *ft, *fy, *fx;
+    int ft_rows, ft_cols, fy_rows, fy_cols, fx_rows, fx_cols, FSEQ, MTPA, D, rope_mode;
+    int next; /* next segment to hand out */
+} PackCtx;
+
+static void pack_one(const PackCtx *c, int s) {
+    const uint16_t *sink_k = c->sink_k, *sink_v = c->sink_v, *mid_k = c->mid_k, *mid_v = c->mid_v;
+    const uint16_t *rec_k = c->rec_k, *rec_v = c->rec_v, *mg_k = c->mg_k, *mg_v = c->mg_v;
+    const int64_t *sink_pos = c->sink_pos, *mid_pos = c->mid_pos, *rec_pos = c->rec_pos;
+    const int64_t *mg_pos = c->mg_pos;
+    uint16_t *k_out = c->k_out, *v_out = c->v_out;
+    int64_t *pos_out = c->pos_out;
+    const int32_t *sk = c->sk, *sg = c->sg, *sl = c->sl, *dst = c->dst;
+    const int64_t *tremap = c->tremap;
+    const float *ft = c->ft, *fy = c->fy, *fx = c->fx;
+    const int ft_rows = c->ft_rows, ft_cols = c->ft_cols, fy_rows = c->fy_rows;
+    const int fy_cols = c->fy_cols, fx_rows = c->fx_rows, fx_cols = c->fx_cols;
+    const int FSEQ = c->FSEQ, MTPA = c->MTPA, D = c->D, rope_mode = c->rope_mode;
     const int ch = D / 2;
-    for (int s = 0; s < nseg; ++s) {
+    do {
         const int kind = sk[s];
-        if (kind < 0) continue;
+        if (kind < 0) break;
         const int len = sl[s];
-        if (len <= 0) continue;
+        if (len <= 0) break;
         const int stride_tok = kind == 3 ? MTPA : FSEQ;
         const int64_t sb = (int64_t)sg[s] * stride_tok * D;
         const int64_t pb = (int64_t)sg[s] * stride_tok * 3;
@@ -577,5 +598,45 @@ void orc_pack(const uint16_t *sink_k, const uint16_t *sink_v, const uint16_t *mi
             memcpy(dv, srcv, (size_t)len * D * 2);
         }
         if (pos_out && srcp) memcpy(pos_out + (int64_t)dst[s] * 3, srcp, (size_t)len * 3 * 8);
+    } while (0);
+}
+
+static void *pack_worker(void *arg) {
+    PackCtx *c = (PackCtx *)arg;
+    for (;;) {
+        const int s = __atomic_fetch_add(&c->next, 1, __ATOMIC_RELAXED);
+        if (s >= c->nseg) return NULL;
+        pack_one(c, s);
     }
+}
+
+/* pools as in orc_update_frames plus merge pools [L*H*MMB, MTPA, D].
+ * k_out/v_out: [T, D]; pos_out: [T, 3] or NULL.  Tables: [rows, cols*2] fp32
+ * or NULL (a NULL remap or all-NULL tables disables RoPE, as in the kernel). */
+void orc_pack(const uint16_t *sink_k, const uint16_t *sink_v, const uint16_t *mid_k,
+              const uint16_t *mid_v, const uint16_t *rec_k, const uint16_t *rec_v,
+              const uint16_t *mg_k, const uint16_t *mg_v, const int64_t *sink_pos,
+              const int64_t *mid_pos, const int64_t *rec_pos, const int64_t *mg_pos,
+              uint16_t *k_out, uint16_t *v_out, int64_t *pos_out, const int32_t *sk,
+              const int32_t *sg, const int32_t *sl, const int32_t *dst, int nseg,
+              const int64_t *tremap, const float *ft, int ft_rows, int ft_cols,
+              const float *fy, int fy_rows, int fy_cols, const float *fx, int fx_rows,
+              int fx_cols, int FSEQ, int MTPA, int D, int rope_mode) {
+    PackCtx c = {sink_k, sink_v, mid_k, mid_v, rec_k, rec_v, mg_k, mg_v, sink_pos, mid_pos,
+                 rec_pos, mg_pos, k_out, v_out, pos_out, sk, sg, sl, dst, nseg, tremap, ft,
+                 fy, fx, ft_rows, ft_cols, fy_rows, fy_cols, fx_rows, fx_cols, FSEQ, MTPA,
+                 D, rope_mode, 0};
+    const int nt = g_threads < nseg ? g_threads : (nseg > 0 ? nseg : 1);
+    if (nt <= 1) {
+        for (int s = 0; s < nseg; ++s) pack_one(&c, s);
+        return;
+    }
+    pthread_t th[256];
+    int started = 0;
+    for (int i = 1; i < nt; ++i) {
+        if (pthread_create(&th[started], NULL, pack_worker, &c) != 0) break;
+        ++started;
+    }
+    pack_worker(&c);
+    for (int i = 0; i < started; ++i) pthread_join(th[i], NULL);
 }

@@ -84,8 +84,15 @@ def lib():
             L.orc_pack.argtypes = ([P] * 19 + [I, P] + [P, I, I] * 3 + [I] * 4)
             L.orc_f32_to_bf16.restype = ctypes.c_uint16
             L.orc_f32_to_bf16.argtypes = [ctypes.c_float]
+            L.orc_set_threads.argtypes = [I]
             _lib = L
     return _lib
+
+
+def set_threads(n: int) -> None:
+    """Threads for the C pack (OpenMP over segments); 1, the default, starts none.
+    Only the timed CPU baseline raises it, to the host's core count."""
+    lib().orc_set_threads(int(n))
 
 
 def _p(a):
