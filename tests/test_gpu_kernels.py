@@ -274,13 +274,14 @@ def test_update_frames_bit_exact(cuda):
                                       .reshape(-1, F, 3), pools[k][2])
 
 
-@pytest.mark.parametrize("W,Hgrid", [(52, 30), (13, 7)])
-def test_merge_accum_bit_exact(cuda, W, Hgrid):
+@pytest.mark.parametrize("W,Hgrid,D", [(52, 30, 128), (13, 7, 128), (13, 7, 64)])
+def test_merge_accum_bit_exact(cuda, W, Hgrid, D):
     """Several blocks of merge frames through the op vs the oracle; accumulators,
-    group ids / divisors / positions and finalized anchors all bit-identical."""
+    group ids / divisors / positions and finalized anchors all bit-identical.
+    head_dim 128 takes the batched 4-dims-per-lane path, 64 the element loop."""
     from pyramidkv import _mega_state_ops as so
     rng = np.random.default_rng(W)
-    H, D, FSEQ, Fb = 3, 128, W * Hgrid, 3
+    H, FSEQ, Fb = 3, W * Hgrid, 3
     kinds = [{"kind": O.SK_MERGE, "patch_size": 2, "capacity": 4},
              {"kind": O.SK_MERGE, "patch_size": 1, "capacity": 2},
              {"kind": O.SK_STRIDE, "interval": 2, "capacity": 4}]
