@@ -16,8 +16,12 @@ rotating set of 8 (inputs + cache pools are larger than L2).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 runs N independent videos, one per rank (weak scaling, no collective on
-the data path).  ``--impl reference`` times the CPU oracle port of the
-reference path on the host cores (rank 0 only).
+the data path); at N = 2, 3, 4, 6 and 8 the line also carries a
+``head_parallel`` object: videos split by heads over groups of n = N ranks
+(n = 4 at N = 8), each layer-step's Q/K/V and output crossing NVLink in two
+NCCL all-to-alls inside the timed region.  ``--head-parallel n`` makes that
+the line's own measurement.  ``--impl reference`` times the CPU oracle port of
+the reference path on the host cores (rank 0 only).
 """
 from __future__ import annotations
 
@@ -56,10 +60,16 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--kernel-case", choices=["attn", "pack", "update"], default=None,
+    ap.add_argument("--kernel-case", choices=["attn", "attn-plain", "pack", "update"],
+                    default=None,
                     help="run one kernel on a standalone steady-state-sized input "
                          "(small device footprint, for profiler captures) and exit")
     ap.add_argument("--kernel-iters", type=int, default=4)
+    ap.add_argument("--head-parallel", type=int, default=0, metavar="n",
+                    help="split each video's heads over groups of n ranks (n divides 12 and "
+                         "the rank count); the line then measures world/n head-parallel videos")
+    ap.add_argument("--hp-steps", type=int, default=3,
+                    help="videos timed by the head-parallel leg added to N > 1 lines")
     return ap.parse_args()
 
 
@@ -402,6 +412,192 @@ def measured_peaks():
             "fallback"
 
 
+# ---------------------------------------------------------------------------
+# head-parallel: one video over a group of n ranks (heads split, NCCL exchange)
+# ---------------------------------------------------------------------------
+class HPWorkload:
+    """One group's video: this rank's heads of the 30 layers behind
+    HeadParallelMegaCache, and this rank's token shard of the rotating
+    Q/K/V sets (the same seeded video on every rank of the group)."""
+
+    @staticmethod
+    def build(device, seed: int, group, merge_fraction=None):
+        import torch
+        import torch.distributed as dist
+        from pyramidkv import head_parallel as hp, policy
+
+        w = HPWorkload.__new__(HPWorkload)
+        w.device = device
+        w.n = dist.get_world_size(group)
+        r = dist.get_rank(group)
+        labels = policy.random_labels(L_, H_, seed=seed, merge_fraction=merge_fraction)
+        comps = policy.compositions_from_labels(labels, "baseline")
+        w.caches = hp.build_head_parallel_caches(
+            L_, H_, D_, FSEQ, 3, 24, 4, comps, group=group, max_attend_chunks=8,
+            device=str(device), sink_time_mapping_mode="window_clamp", sink_time_clamp_min=18,
+            sink_time_clamp_max=21, spatial_width=W_, spatial_height=HG_, freqs=rope_table(D_))
+        w.ctx = w.caches[0].local.ctx
+        w.init_states = w.ctx.states_bytes.clone()
+        w.ctx.token_counter = torch.zeros(1, dtype=torch.int64, device=device)
+        t0, t1 = hp.token_range(r, w.n, FRAMES_PER_BLOCK * FSEQ)
+        g = torch.Generator(device=device).manual_seed(1000 + seed)
+        shape = (1, FRAMES_PER_BLOCK * FSEQ, H_, D_)
+        w.sets = []
+        for _ in range(N_SETS):
+            full = [torch.randn(shape, generator=g, device=device, dtype=torch.bfloat16)
+                    for _ in range(3)]
+            w.sets.append(tuple(x[:, t0:t1].contiguous() for x in full))
+        return w
+
+    def reset(self):
+        Workload.reset(self)
+
+
+def run_video_hp(w, frames: int, inputs=None, hooks=None):
+    """One head-parallel video: per layer-step ``step(q, k, v)`` (Q/K/V in one
+    exchange, update + attend on this rank's heads, output exchanged back)."""
+    i = 0
+    for blk in range(frames // FRAMES_PER_BLOCK):
+        start = blk * FRAMES_PER_BLOCK * FSEQ
+        for mode in PASSES:
+            for layer in range(L_):
+                q, k, v = inputs(i) if inputs is not None else w.sets[i % N_SETS]
+                if hooks:
+                    hooks[0](i)
+                out = w.caches[layer].step(q, k, v, start, cache_update_mode=mode)
+                if hooks:
+                    hooks[2](i, out)
+                i += 1
+    return i
+
+
+def head_parallel_measure(args, rank: int, world: int, local: int, n: int, steps: int,
+                          warmup: int, with_e2e: bool):
+    """world/n videos, each split by heads over n ranks; returns the measured
+    dict on every rank (rank 0 prints it)."""
+    import torch
+    import torch.distributed as dist
+    if H_ % n or world % n:
+        raise ValueError(f"head-parallel over {n} ranks needs n | {H_} and n | {world}")
+    groups = [dist.new_group(list(range(g * n, (g + 1) * n))) for g in range(world // n)]
+    gi = rank // n
+    dev = torch.device("cuda", local)
+    w = HPWorkload.build(dev, seed=args.seed + gi, group=groups[gi],
+                         merge_fraction=args.merge_fraction)
+    for _ in range(warmup):
+        w.reset()
+        run_video_hp(w, args.frames)
+    torch.cuda.synchronize()
+    w.ctx.check_status()
+    w.ctx.token_counter.zero_()
+    n_ls = layer_steps(args.frames)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_ls * steps)]
+    cur = [0]
+
+    def stage(name):
+        ev[cur[0]][1 if name == "exchanged_in" else 2].record()
+    for c in w.caches:
+        c.on_stage = stage
+    hooks = (lambda i: ev[cur[0]][0].record(), None,
+             lambda i, out: (ev[cur[0]][3].record(), cur.__setitem__(0, cur[0] + 1)))
+    dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks_start(local)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        w.reset()
+        run_video_hp(w, args.frames, hooks=hooks)
+    t1.record()
+    torch.cuda.synchronize()
+    clocks = clocks_stop(clk)
+    for c in w.caches:
+        c.on_stage = None
+    ms = max_over_ranks(t0.elapsed_time(t1), world)
+    tot = n_ls * steps
+    ex_in = sum(e[0].elapsed_time(e[1]) for e in ev) * 1e3 / tot
+    cache = sum(e[1].elapsed_time(e[2]) for e in ev) * 1e3 / tot
+    ex_out = sum(e[2].elapsed_time(e[3]) for e in ev) * 1e3 / tot
+    shard = w.sets[0][0]
+    lt = shard.shape[1]
+    bytes_in = 3 * shard.numel() * 2 * (n - 1) // n   # Q/K/V leaving this rank
+    bytes_out = shard.numel() * 2 * (n - 1) // n
+    res = {"n": n, "groups": world // n, "videos": world // n, "steps": steps,
+           "warmup": warmup, "ms_per_video": ms / steps,
+           "value": (world // n) * steps * args.frames / (ms / 1e3), "unit": "latent frames/s",
+           "scaling": "strong within a group (one video's heads over n GPUs)",
+           "us_per_layer_step": ms * 1e3 / tot,
+           "breakdown_us_per_layer_step_rank": {
+               "exchange_in (pack Q/K/V + all_to_all)": ex_in,
+               "cache (update + plan/pack + attention)": cache,
+               "exchange_out (all_to_all + scatter O)": ex_out},
+           "heads_per_rank": H_ // n, "tokens_per_rank": lt,
+           "nvlink_bytes_per_layer_step_rank": {"qkv": bytes_in, "out": bytes_out},
+           "collective": "torch.distributed all_to_all_single (NCCL), Q/K/V together, O back",
+           "clocks": clocks}
+    if with_e2e:
+        from pyramidkv.host_staging import HostStaging
+        host = [tuple(x.cpu().pin_memory() for x in s_) for s_ in w.sets]
+        host_out = [torch.empty(tuple(shard.shape), dtype=torch.bfloat16).pin_memory()
+                    for _ in range(2)]
+        st = HostStaging(w.sets[0], dev, depth=2)
+        pos = [0]
+
+        def inputs(i):
+            if pos[0] == 0:
+                st.put(host[0])
+            if pos[0] + 1 < n_ls:
+                st.put(host[(pos[0] + 1) % N_SETS])
+            return st.get()
+
+        def after(i, out):
+            st.done(out, host_out[pos[0] % 2])
+            pos[0] += 1
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        w.reset()
+        run_video_hp(w, args.frames, inputs=inputs, hooks=(lambda i: None, None, after))
+        torch.cuda.current_stream().wait_stream(st.copy_out)
+        e1.record()
+        torch.cuda.synchronize()
+        ems = max_over_ranks(e0.elapsed_time(e1), world)
+        res["e2e"] = {"value": (world // n) * args.frames / (ems / 1e3), "unit": "latent frames/s",
+                      "h2d_bytes_per_step": 3 * shard.numel() * 2 * n_ls * world,
+                      "d2h_bytes_per_step": shard.numel() * 2 * n_ls * world,
+                      "ms_per_step": ems,
+                      "path": "HeadParallelMegaCache.step with each rank's pinned host token "
+                              "shard of Q/K/V in and O out per layer-step (HostStaging)"}
+    res["device_status"] = w.ctx.check_status()
+    del w
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_head_parallel_line(args, rank: int, world: int, local: int):
+    """``--head-parallel n``: the line measures world/n head-parallel videos."""
+    n = args.head_parallel
+    res = head_parallel_measure(args, rank, world, local, n, args.steps, args.warmup,
+                                with_e2e=not args.no_e2e)
+    if rank != 0:
+        return
+    line = {"metric": METRIC, "value": res["value"], "unit": "latent frames/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_video"], "higher_is_better": True,
+            "scaling": "strong" if world == n else "weak", "vs_baseline": None,
+            "dtype": "bf16",
+            "data": ("synthetic: seeded N(0,1) bf16 Q/K/V per layer-step, seeded random [30,12] "
+                     "label matrix, model RoPE table; no checkpoint (cache path only)"),
+            "config": dict(workload_config(args), parallelism=f"head-parallel x{n}, "
+                           f"{world // n} video(s)"),
+            "us_per_layer_step": res["us_per_layer_step"], "head_parallel": res,
+            "e2e": res.get("e2e"), "clocks": res["clocks"],
+            "gpu_launches": layer_steps(args.frames) * args.steps * 7,
+            "device_status": res["device_status"]}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, rank: int, world: int, local: int):
     import torch
     torch.cuda.set_device(local)
@@ -476,6 +672,13 @@ def run_ours(args, rank: int, world: int, local: int):
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         fps_cpu, detail = cpu_sample(args)
         line["cpu_baseline"] = cpu_baseline_json(fps_cpu, detail, os.cpu_count())
+    if world > 1 and args.hp_steps > 0:
+        n = world if H_ % world == 0 else (4 if world % 4 == 0 else 0)
+        if n:
+            del w
+            torch.cuda.empty_cache()
+            line["head_parallel"] = head_parallel_measure(
+                args, rank, world, local, n, args.hp_steps, 1, with_e2e=False)
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -498,12 +701,19 @@ def run_kernel_case(args):
     T = int(cu[-1])
     ops = _ops.ops()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    if args.kernel_case == "attn":
+    if args.kernel_case in ("attn", "attn-plain"):
+        # attn: the SM-balanced path MegaCache.attend runs (workspace given);
+        # attn-plain: one CTA per (segment, query-tile pair), no workspace
         q = torch.randn(1, C * FSEQ, H_, D_, generator=g).to(dev, torch.bfloat16)
         k = torch.randn(T, D_, generator=g).to(dev, torch.bfloat16)
         v = torch.randn(T, D_, generator=g).to(dev, torch.bfloat16)
         cud = cu.to(dev)
-        run = lambda: ops.pkv_attention(q[0], k, v, cud, C, FSEQ, D_ ** -0.5)  # noqa: E731
+        if args.kernel_case == "attn":
+            ws = torch.zeros(int(ops.pkv_attention_ws_bytes(C, H_, FSEQ)), dtype=torch.uint8,
+                             device=dev)
+            run = lambda: ops.pkv_attention_ws(q[0], k, v, cud, C, FSEQ, D_ ** -0.5, ws)  # noqa
+        else:
+            run = lambda: ops.pkv_attention(q[0], k, v, cud, C, FSEQ, D_ ** -0.5)  # noqa: E731
         work, unit = 4.0 * FSEQ * D_ * T, "FLOP"
     elif args.kernel_case == "update":
         # one layer with a third of its heads merge heads, after 30 blocks; a
@@ -586,7 +796,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     try:
-        run_ours(args, rank, world, local)
+        if args.head_parallel:
+            run_head_parallel_line(args, rank, world, local)
+        else:
+            run_ours(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist

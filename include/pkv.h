@@ -221,6 +221,31 @@ int pkv_attention(const uint16_t *q, int64_t q_row_stride, int64_t q_head_stride
                   int64_t o_row_stride, int64_t o_head_stride, pkv_stream_t stream);
 
 /*
+ * pkv_attention with a caller-owned workspace, which lets the kernel balance
+ * the work over the SMs: one persistent CTA per SM, the longest
+ * (segment, query-tile pair) units run whole and the rest are cut into equal
+ * per-SM shares, a unit cut between SMs being finished by whichever share
+ * ends last (fp32 partials in the workspace; no SM waits for another).
+ * Results match pkv_attention within the fp32-accumulation tolerance (the
+ * split units sum their keys in a different order).  workspace: device
+ * memory of at least pkv_attention_workspace_bytes(...) bytes, 256-byte
+ * aligned, zero-filled before its first use; every launch leaves it ready for
+ * the next (its counters back at zero), so it is reused without clearing.
+ * Launches sharing a workspace must not overlap on the GPU.  A launch that
+ * ended on a device timeout (PKV_ST_TIMEOUT) can leave counters set: zero the
+ * workspace again before reuse.  workspace == NULL runs pkv_attention.
+ * Replaces: flash_attn.flash_attn_varlen_func at pyramidkv/_mega_cache.py:550-559
+ * (as pkv_attention; MegaCache.attend uses this path with the cache's scratch).
+ */
+int64_t pkv_attention_workspace_bytes(int num_chunks, int num_heads, int rows_per_chunk);
+int pkv_attention_ws(const uint16_t *q, int64_t q_row_stride, int64_t q_head_stride,
+                     const uint16_t *k, const uint16_t *v, int64_t kv_rows,
+                     const int32_t *cu_seqlens_k, int num_chunks, int num_heads,
+                     int rows_per_chunk, int head_dim, float softmax_scale, uint16_t *out,
+                     int64_t o_row_stride, int64_t o_head_stride, void *workspace,
+                     int64_t workspace_bytes, pkv_stream_t stream);
+
+/*
  * One layer's MegaCache.update on the device: restore the committed
  * valid_count / recent pool, route each head's frames to sink or recent (FIFO
  * on overflow), run the strategy state machine and the middle / merge writes
@@ -312,6 +337,22 @@ int pkv_rope_q(const uint16_t *x, int64_t x_tok_stride, int64_t x_head_stride, u
                int head_dim, int64_t start_frame, int frames, int grid_h, int grid_w,
                const double *freqs_t, int t_rows, int t_cols, const double *freqs_y, int y_rows,
                int y_cols, const double *freqs_x, int x_rows, int x_cols, pkv_stream_t stream);
+
+/*
+ * Head-parallel exchange layout copy (around the NCCL all-to-all of a layer
+ * step split over ranks by heads): for each source i < count (<= 4), token
+ * t < tokens and group g < groups, copy the group_elems bf16 elements at
+ * srcs[i] + t*src_tok_strides[i] + g*src_group_strides[i] to
+ * dst + t*dst_tok_stride + g*dst_group_stride + i*dst_src_stride (all in
+ * elements).  Packs Q, K and V of a token shard into a by-destination send
+ * buffer in one pass, and scatters a received attention output back into
+ * the [tokens, heads, D] layout.  16-byte copies when every address and
+ * stride allows.  No counterpart in the reference (it runs on one GPU).
+ */
+int pkv_chunk_copy(const uint16_t *const *srcs, const int64_t *src_tok_strides,
+                   const int64_t *src_group_strides, int count, uint16_t *dst,
+                   int64_t dst_tok_stride, int64_t dst_group_stride, int64_t dst_src_stride,
+                   int64_t tokens, int groups, int group_elems, pkv_stream_t stream);
 
 /* ---- AdaptiveKVCache / CppStrategyManager ops (not on the MegaCache path) ----
  * Same bytes as the reference's kernels; launched on `stream` (the

@@ -132,6 +132,10 @@ class PyramidKVCacheManager : public torch::CustomClassHolder {
     recent_pos_.zero_();
     merge_tc_.zero_();
     acc_ng_.zero_();
+    // not in the reference: the attention workspace's arrival counters live
+    // in the scratch; a launch that ended on a device timeout can leave them
+    // set, so a reset starts them from zero again
+    if (scratch_.defined()) scratch_.zero_();
   }
 
   void set_strategy(int64_t l, int64_t h, int64_t kind, Tensor params) {
@@ -627,6 +631,69 @@ Tensor op_attention(Tensor q, Tensor k, Tensor v, Tensor cu, int64_t num_chunks,
   return out;
 }
 
+// pkv_attention with a caller-owned workspace (uint8, zero-filled before its
+// first use, at least pkv_attention_workspace_bytes): the SM-balanced path.
+Tensor op_attention_ws(Tensor q, Tensor k, Tensor v, Tensor cu, int64_t num_chunks,
+                       int64_t rows_per_chunk, double scale, Tensor workspace) {
+  TORCH_CHECK(workspace.is_cuda() && workspace.dtype() == at::kByte &&
+                  workspace.is_contiguous() && workspace.device() == q.device(),
+              "pkv_attention_ws: workspace must be a contiguous uint8 tensor on q's device");
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && cu.is_cuda(),
+              "pkv_attention: tensors must be CUDA");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 &&
+                  v.scalar_type() == at::kBFloat16,
+              "pkv_attention: q/k/v must be bf16");
+  TORCH_CHECK(cu.dtype() == at::kInt, "pkv_attention: cu_seqlens_k must be int32");
+  TORCH_CHECK(q.dim() == 3, "pkv_attention: q must be [num_chunks*rows, H, D]");
+  const int64_t H = q.size(1), D = q.size(2);
+  TORCH_CHECK(q.size(0) == num_chunks * rows_per_chunk, "pkv_attention: q rows mismatch");
+  TORCH_CHECK(cu.numel() >= num_chunks * H + 1, "pkv_attention: cu_seqlens_k too short");
+  const int64_t need = pkv_attention_workspace_bytes(int(num_chunks), int(H), int(rows_per_chunk));
+  TORCH_CHECK(workspace.numel() >= need, "pkv_attention_ws: workspace needs ", need, " bytes");
+  const c10::cuda::CUDAGuard g(q.device());
+  auto qq = q.stride(2) == 1 ? q : q.contiguous();
+  auto kk = k.reshape({-1, D}).contiguous(), vv = v.reshape({-1, D}).contiguous();
+  auto cc = cu.contiguous();
+  auto out = at::empty({q.size(0), H, D}, q.options());
+  check_rc(pkv_attention_ws(reinterpret_cast<const uint16_t*>(qq.data_ptr()), qq.stride(0),
+                            qq.stride(1), reinterpret_cast<const uint16_t*>(kk.data_ptr()),
+                            reinterpret_cast<const uint16_t*>(vv.data_ptr()), kk.size(0),
+                            cc.data_ptr<int32_t>(), int(num_chunks), int(H), int(rows_per_chunk),
+                            int(D), float(scale), reinterpret_cast<uint16_t*>(out.data_ptr()),
+                            out.stride(0), out.stride(1), workspace.data_ptr(), workspace.numel(),
+                            stream_of(qq)),
+           "pkv_attention_ws");
+  return out;
+}
+
+int64_t op_attention_ws_bytes(int64_t num_chunks, int64_t num_heads, int64_t rows_per_chunk) {
+  return pkv_attention_workspace_bytes(int(num_chunks), int(num_heads), int(rows_per_chunk));
+}
+
+// Head-parallel exchange layout copy (pkv_chunk_copy): strides in elements
+// relative to each tensor's data pointer (views welcome).
+void op_chunk_copy(std::vector<Tensor> srcs, std::vector<int64_t> src_ts,
+                   std::vector<int64_t> src_gs, Tensor dst, int64_t dst_ts, int64_t dst_gs,
+                   int64_t dst_is, int64_t tokens, int64_t groups, int64_t group_elems) {
+  TORCH_CHECK(!srcs.empty() && srcs.size() <= 4 && src_ts.size() == srcs.size() &&
+                  src_gs.size() == srcs.size(),
+              "pkv_chunk_copy: 1-4 sources with one token and one group stride each");
+  TORCH_CHECK(dst.is_cuda() && dst.scalar_type() == at::kBFloat16,
+              "pkv_chunk_copy: dst must be a bf16 CUDA tensor");
+  const uint16_t* ptrs[4] = {};
+  for (size_t i = 0; i < srcs.size(); ++i) {
+    TORCH_CHECK(srcs[i].is_cuda() && srcs[i].scalar_type() == at::kBFloat16 &&
+                    srcs[i].device() == dst.device(),
+                "pkv_chunk_copy: sources must be bf16 tensors on dst's device");
+    ptrs[i] = reinterpret_cast<const uint16_t*>(srcs[i].data_ptr());
+  }
+  const c10::cuda::CUDAGuard g(dst.device());
+  check_rc(pkv_chunk_copy(ptrs, src_ts.data(), src_gs.data(), int(srcs.size()),
+                          reinterpret_cast<uint16_t*>(dst.data_ptr()), dst_ts, dst_gs, dst_is,
+                          tokens, int(groups), int(group_elems), stream_of(dst)),
+           "pkv_chunk_copy");
+}
+
 // 3D RoPE of a query block of one sample: x [tokens, H, D] bf16 (last dim
 // contiguous), tables float64 [rows, cols * 2] (re, im) for the t / y / x
 // parts; returns a new [tokens, H, D] tensor (causal_model.py:30-63).
@@ -946,6 +1013,12 @@ TORCH_LIBRARY(adahead, m) {
         "Tensor q, float softmax_scale) -> Tensor");
   m.def("pkv_attention(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens_k, int num_chunks, "
         "int rows_per_chunk, float softmax_scale) -> Tensor");
+  m.def("pkv_attention_ws(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens_k, int num_chunks, "
+        "int rows_per_chunk, float softmax_scale, Tensor(a!) workspace) -> Tensor");
+  m.def("pkv_attention_ws_bytes(int num_chunks, int num_heads, int rows_per_chunk) -> int");
+  m.def("pkv_chunk_copy(Tensor[] srcs, int[] src_tok_strides, int[] src_group_strides, "
+        "Tensor(a!) dst, int dst_tok_stride, int dst_group_stride, int dst_src_stride, "
+        "int tokens, int groups, int group_elems) -> ()");
   m.def("pkv_status(__torch__.torch.classes.adahead.PyramidKVCacheManager mgr) -> int");
   m.def("pkv_rope_rounding(int mode) -> int");
   m.def("pkv_rope_q(Tensor x, Tensor ft, Tensor fy, Tensor fx, int start_frame, int frames, "
@@ -967,6 +1040,8 @@ TORCH_LIBRARY_IMPL(adahead, CUDA, m) {
   m.impl("pkv_attend_pack", op_attend_pack);
   m.impl("pkv_attend_attention", op_attend_attention);
   m.impl("pkv_attention", op_attention);
+  m.impl("pkv_attention_ws", op_attention_ws);
+  m.impl("pkv_chunk_copy", op_chunk_copy);
 }
 
 TORCH_LIBRARY_IMPL(adahead, CompositeExplicitAutograd, m) {
@@ -975,6 +1050,7 @@ TORCH_LIBRARY_IMPL(adahead, CompositeExplicitAutograd, m) {
   m.impl("mega_plan", mega_plan);
   m.impl("mega_plan_multi", mega_plan_multi);
   m.impl("pkv_status", op_status);
+  m.impl("pkv_attention_ws_bytes", op_attention_ws_bytes);
   m.impl("pkv_rope_rounding", op_rope_rounding);
 }
 

@@ -49,17 +49,44 @@ extern "C" int pkv_attend_pack(const pkv_cache_t* c, const uint8_t* states_layer
                      ft_cols, fy, fy_rows, fy_cols, fx, fx_rows, fx_cols, s);
 }
 
+namespace {
+
+// Ragged attention over the cache's last pack; with `use_scratch` the
+// cache's scratch lends the attention kernel its split-unit workspace.
+int attend_attention(const pkv_cache_t* c, const uint16_t* q, int64_t q_tok_stride,
+                     int64_t q_head_stride, int num_chunks, float scale, uint16_t* out,
+                     int64_t o_tok_stride, int64_t o_head_stride, bool use_scratch,
+                     cudaStream_t stream) {
+  if (!c || !q || !out || !c->cu_seqlens_k || !c->k_flat || !c->v_flat) return PKV_EINVAL;
+  if (num_chunks <= 0) return PKV_OK;
+  if (num_chunks > c->max_attend_chunks) return PKV_ECAPACITY;
+  AttnWorkspace ws{};
+  const AttnWorkspace* wsp = nullptr;
+  if (use_scratch && c->scratch != nullptr) {
+    const ScratchLayout sl = scratch_layout(c);
+    if (c->scratch_bytes >= sl.bytes) {
+      char* scr = static_cast<char*>(c->scratch);
+      ws.part = reinterpret_cast<float*>(scr + sl.attn_part);
+      ws.cnt = reinterpret_cast<int32_t*>(scr + sl.attn_cnt);
+      ws.cnt_units = attn_units(c);
+      wsp = &ws;
+    }
+  }
+  return launch_attention(q, q_tok_stride, q_head_stride, c->k_flat, c->v_flat,
+                          c->max_pack_tokens, c->cu_seqlens_k, num_chunks, c->num_heads,
+                          c->frame_seqlen, c->head_dim, scale, out, o_tok_stride, o_head_stride,
+                          c->status, wsp, stream);
+}
+
+}  // namespace
+
 extern "C" int pkv_attend_attention(const pkv_cache_t* c, const uint16_t* q,
                                     int64_t q_tok_stride, int64_t q_head_stride, int num_chunks,
                                     float scale, uint16_t* out, int64_t o_tok_stride,
                                     int64_t o_head_stride, pkv_stream_t stream) {
-  if (!c || !q || !out || !c->cu_seqlens_k || !c->k_flat || !c->v_flat) return PKV_EINVAL;
-  if (num_chunks <= 0) return PKV_OK;
-  if (num_chunks > c->max_attend_chunks) return PKV_ECAPACITY;
-  return launch_attention(q, q_tok_stride, q_head_stride, c->k_flat, c->v_flat,
-                          c->max_pack_tokens, c->cu_seqlens_k, num_chunks, c->num_heads,
-                          c->frame_seqlen, c->head_dim, scale, out, o_tok_stride, o_head_stride,
-                          c->status, static_cast<cudaStream_t>(stream));
+  return attend_attention(c, q, q_tok_stride, q_head_stride, num_chunks, scale, out,
+                          o_tok_stride, o_head_stride, /*use_scratch=*/true,
+                          static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pkv_attend(const pkv_cache_t* c, const uint8_t* states_layer, int layer,
@@ -164,6 +191,7 @@ extern "C" int pkv_attend_noalloc(const pkv_cache_t* c, const uint8_t* states_la
   rc = launch_pack(c, sk, sg, sln, dst, int(n), rope ? tremap : nullptr, ft, ft_rows, ft_cols,
                    fy, fy_rows, fy_cols, fx, fx_rows, fx_cols, s);
   if (rc != PKV_OK) return rc;
-  return pkv_attend_attention(c, q, q_tok_stride, q_head_stride, num_chunks, scale, out,
-                              o_tok_stride, o_head_stride, stream);
+  // one CTA per attention unit: the split-unit workspace would be scratch
+  return attend_attention(c, q, q_tok_stride, q_head_stride, num_chunks, scale, out,
+                          o_tok_stride, o_head_stride, /*use_scratch=*/false, s);
 }

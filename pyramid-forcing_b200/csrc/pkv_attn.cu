@@ -29,7 +29,12 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
 #include "pkv_common.cuh"
+#include "pkv_internal.h"
 
 namespace pkv {
 
@@ -102,6 +107,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(su32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+// Pull a tile of a tensor into L2 ahead of its load (no shared memory, no
+// completion to wait for).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -259,6 +272,28 @@ __host__ __device__ constexpr uint32_t idesc_bf16(bool b_mn_major) {
          (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
 }
 
+// ---------------------------------------------------------------------------
+// Work decomposition.  A unit is (segment, pair of 128-row query tiles); the
+// last unit of a segment holds one tile when rows_per_chunk / 128 rounds up
+// to an odd count (1560 rows: 6 pairs + one 24-row tile).  Units are ordered
+// segment-major, longest segment first, so the units of one segment are
+// neighbours and read its K/V from HBM once.
+//
+// Without a partial-result workspace (AttnArgs::part == nullptr) the grid has
+// one CTA per unit.  With it the grid is one persistent CTA per SM:
+//   * phase 1: CTA b runs unit b whole (the longest units, side by side as in
+//     the one-CTA-per-unit grid);
+//   * phase 2: the remaining units are laid end to end on a cost axis (K/V
+//     steps x a per-step weight: a pair step costs more than a lone-tile
+//     step) and cut into one contiguous range per CTA, sized so that every
+//     CTA's phase-1 + phase-2 cost is the same.  A range edge that falls
+//     inside a unit splits the unit's K/V steps between CTAs (stream-K).
+// Each piece of a split unit writes its unnormalised O, row maximum m and
+// row sum l (fp32) to a per-CTA slot of the workspace; per (unit, tile, warp)
+// an arrival counter picks the last piece to finish, which combines
+//   O = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p,  M = max_p m_p
+// and stores the bf16 rows.  No CTA waits for another.
+// ---------------------------------------------------------------------------
 struct AttnArgs {
   const int32_t* cu;
   int n_seg, H, rows_per_chunk, m_tiles;
@@ -266,33 +301,46 @@ struct AttnArgs {
   uint16_t* out;
   int64_t o_row_stride, o_head_stride;
   int32_t* status;
+  float* part;     // [kMaxCtas][2 slots][2 tiles][kPartFloats] partials, or nullptr
+  int32_t* cnt;    // [units][2 tiles][4 warps] arrival counters, zero between launches
+  int w_pair, w_single, w_fixed;  // cost model: phase-1 step weights, per-piece cost
+  int w2_pair, w2_single;         // phase-2 step weights
+  int prefetch;                   // K/V steps pulled into L2 ahead of their loads
 };
 
 // ---------------------------------------------------------------------------
-// Two query tiles per CTA (ping-pong).  One CTA per (segment, pair of 128-row
-// query tiles); both tiles stream the same K/V tiles.  Warp 0: TMA; warp 1:
-// tcgen05.mma issue; warps 2-5: softmax of tile 0; warps 6-9: softmax of
-// tile 1.  TMEM: S0 | S1 | O0 | O1, 128 columns each; P_t overwrites S_t as
-// bf16 pairs.  MMA issue order per K/V tile j:
+// Two query tiles per CTA (ping-pong).  Warp 0: TMA; warp 1: tcgen05.mma
+// issue; warps 2-5: softmax of tile 0; warps 6-9: softmax of tile 1.  TMEM:
+// S0 | S1 | O0 | O1, 128 columns each; P_t overwrites S_t as bf16 pairs.  MMA
+// issue order per K/V tile j:
 //   PV0(j-1)  QK0(j)  PV1(j-1)  QK1(j)
 // so while one softmax warpgroup works on S_t(j) the tensor pipe runs the
 // other tile's P·V and Q·K^T.  The tensor pipe executes one CTA's MMAs in
 // issue order, so QK_t(j) (which overwrites S_t) runs after PV_t(j-1) (which
 // reads P_t from the same columns), and the commit that signals S_t(j) also
 // covers PV_t(j-1): a softmax warpgroup that sees S_t(j) may rescale O_t.
+// Across pieces of a persistent CTA the barriers keep counting: the K/V ring
+// by global step, S/P by per-tile step, O-final by per-tile piece, and a
+// q_empty commit after a piece's last Q·K^T lets the next piece's Q load.
+// The first P·V of a piece (which overwrites O_t) waits for P_t of that
+// piece, which the softmax warps post only after reading O_t of the last one.
 // Softmax: exp2 of 2 of every 5 column pairs on the FMA pipe (exp2_poly2),
 // the rest on MUFU; the last (partial) K tile uses MUFU only, which maps the
 // masked -inf scores to exactly 0.
 // ---------------------------------------------------------------------------
 constexpr int kThreads2 = 320;
 constexpr int kStages2 = 2;
-constexpr int kMaxSegLens = 1024;  // segment lengths staged in shared memory
+constexpr int kMaxSegLens = 1024;    // segment lengths / ranks staged in shared memory
+constexpr int kMaxCtas = kAttnMaxCtas;  // persistent grid bound (>= SM count)
+constexpr int kMaxSplitUnits = 1024;     // phase-2 units staged in shared memory
+constexpr int64_t kPartFloats = kAttnPartFloats;  // O columns x rows, m, l, per-warp unit ids
+static_assert(kAttnPartFloats == 130 * kBM + 32, "partial block layout");
 
 struct __align__(1024) AttnSmem2 {
   uint8_t q[2][kTileBytes];
   uint8_t k[kStages2][kTileBytes];
   uint8_t v[kStages2][kTileBytes];
-  uint64_t q_full;
+  uint64_t q_full, q_empty;
   uint64_t kv_full[kStages2];
   uint64_t kv_empty[kStages2];
   uint64_t s_full[2];
@@ -301,8 +349,11 @@ struct __align__(1024) AttnSmem2 {
   uint64_t mma_drain;
   uint32_t tmem_base;
   int abort;
-  int seg, unit;
+  int seg1;                        // this CTA's phase-1 segment (lengths not staged)
+  int64_t pre2[kMaxSplitUnits + 1];  // phase-2 cost prefix
+  int64_t bnd[kMaxCtas + 1];         // CTA range bounds on the phase-2 axis
   int seg_len[kMaxSegLens];
+  int16_t order[kMaxSegLens];        // segment of each length rank
 };
 
 // Row max over 128 raw scores held as bits (tree of 3-input max).
@@ -353,6 +404,126 @@ __device__ __forceinline__ void softmax_chunk(const uint32_t (&s)[32], f2 scale2
   }
 }
 
+// One piece of work: K/V steps [k0, k1) of unit q (segment seg, query tiles
+// 2*unit and 2*unit+1 of each chunk's rows).
+struct Piece {
+  int q, seg, unit, ntile, k0, k1, kv0, lk, whole;
+};
+
+// Read-only view of the schedule every CTA computes in shared memory.
+struct Sched {
+  const AttnSmem2* sm;
+  const int32_t* cu;
+  int m_tiles, w_pair, w_single;  // phase-2 step weights
+  int U, NU, G, n1, n2;  // units per segment, units, grid, phase-1 units, phase-2 units
+  bool staged;           // segment lengths and ranks in shared memory
+
+  __device__ int seg_len(int s) const { return staged ? sm->seg_len[s] : cu[s + 1] - cu[s]; }
+  // Segment, query-tile pair, tile count and K/V steps of unit q.
+  __device__ void unit(int q, int& seg, int& u, int& ntile, int& nkv) const {
+    const int r = q / U;
+    u = q - r * U;
+    seg = staged ? int(sm->order[r]) : sm->seg1;
+    ntile = (2 * u + 1 < m_tiles) ? 2 : 1;
+    nkv = (seg_len(seg) + kBN - 1) / kBN;
+  }
+  __device__ int weight(int ntile) const { return ntile == 2 ? w_pair : w_single; }
+  // K/V step at which cost position B cuts phase-2 unit q2.
+  __device__ int cut(int64_t B, int q2, int w, int nkv) const {
+    const int64_t base = sm->pre2[q2];
+    if (B <= base) return 0;
+    const int64_t k = (B - base) / w;
+    return k >= nkv ? nkv : int(k);
+  }
+  __device__ void fill(Piece& p, int q, int seg, int u, int ntile, int k0, int k1,
+                       int nkv) const {
+    p.q = q;
+    p.seg = seg;
+    p.unit = u;
+    p.ntile = ntile;
+    p.k0 = k0;
+    p.k1 = k1;
+    p.kv0 = cu[seg];
+    p.lk = seg_len(seg);
+    p.whole = (k0 == 0 && k1 == nkv) ? 1 : 0;
+  }
+  // First phase-2 unit whose cost interval ends after position B.
+  __device__ int first_unit_after(int64_t B) const {
+    int lo = 0, hi = n2;  // smallest q2 with pre2[q2 + 1] > B
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (sm->pre2[mid + 1] > B)
+        hi = mid;
+      else
+        lo = mid + 1;
+    }
+    return lo;
+  }
+  // Last CTA whose range starts at or before position B.
+  __device__ int cta_at(int64_t B) const {
+    int lo = 0, hi = G - 1;  // largest j with bnd[j] <= B
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sm->bnd[mid] <= B)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    return lo;
+  }
+};
+
+// Pieces of CTA b in order: its phase-1 unit, then its phase-2 range.
+struct Cursor {
+  int stage, q2;
+};
+
+__device__ __forceinline__ bool next_piece(const Sched& S, int b, Cursor& cur, Piece& p) {
+  int seg, u, ntile, nkv;
+  if (cur.stage == 0) {
+    cur.stage = 1;
+    cur.q2 = S.n2 > 0 ? S.first_unit_after(S.sm->bnd[b]) : 0;
+    if (b < S.n1) {
+      S.unit(b, seg, u, ntile, nkv);
+      if (nkv > 0) {
+        S.fill(p, b, seg, u, ntile, 0, nkv, nkv);
+        return true;
+      }
+    }
+  }
+  if (S.n2 == 0) return false;
+  const int64_t lo = S.sm->bnd[b], hi = S.sm->bnd[b + 1];
+  while (cur.q2 < S.n2 && S.sm->pre2[cur.q2] < hi) {
+    const int q2 = cur.q2++;
+    S.unit(S.n1 + q2, seg, u, ntile, nkv);
+    if (nkv == 0) continue;
+    const int w = S.weight(ntile);
+    const int k0 = S.cut(lo, q2, w, nkv), k1 = S.cut(hi, q2, w, nkv);
+    if (k1 > k0) {
+      S.fill(p, S.n1 + q2, seg, u, ntile, k0, k1, nkv);
+      return true;
+    }
+  }
+  return false;
+}
+
+// Store one warp's 32 rows x 128 columns of fp32 as normalised bf16 rows.
+__device__ __forceinline__ void store_row32(uint16_t* dst, const uint32_t (&o)[32], float inv) {
+#pragma unroll
+  for (int e = 0; e < 32; e += 8) {
+    uint4 w;
+    w.x = pack_bf16x2(__uint_as_float(o[e + 0]) * inv, __uint_as_float(o[e + 1]) * inv);
+    w.y = pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+    w.z = pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+    w.w = pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+    *reinterpret_cast<uint4*>(dst + e) = w;
+  }
+}
+
+__device__ __forceinline__ float* part_block(const AttnArgs& a, int cta, int slot, int t) {
+  return a.part + (size_t(cta) * 4 + slot * 2 + t) * kPartFloats;
+}
+
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_tc2_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
@@ -362,18 +533,28 @@ __global__ void __launch_bounds__(kThreads2, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort = &sm.abort;
-  // Segment-major: the units of one segment are adjacent CTAs, so they run
-  // side by side and read its K/V from HBM once (scheduling the odd last
-  // tiles after all pairs measured slower: their K/V had left L2).
-  const int units = (a.m_tiles + 1) >> 1;
-  const int order = blockIdx.x / units;
-  const int unit_of_block = blockIdx.x - order * units;
+  const int b = blockIdx.x;
+
+  Sched S;
+  S.sm = &sm;
+  S.cu = a.cu;
+  S.m_tiles = a.m_tiles;
+  S.w_pair = a.w2_pair;
+  S.w_single = a.w2_single;
+  S.U = (a.m_tiles + 1) >> 1;
+  S.NU = a.n_seg * S.U;
+  S.G = gridDim.x;
+  S.staged = a.n_seg <= kMaxSegLens;
+  const bool split = a.part != nullptr && S.staged && S.NU > S.G &&
+                     S.NU - S.G <= kMaxSplitUnits && S.G <= kMaxCtas;
+  S.n1 = split ? S.G : S.NU;
+  S.n2 = split ? S.NU - S.G : 0;
 
   if (threadIdx.x == 0) {
-    sm.seg = -1;
-    sm.unit = unit_of_block;
+    sm.seg1 = -1;
     sm.abort = 0;
     mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
     for (int s = 0; s < kStages2; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
@@ -386,21 +567,94 @@ __global__ void __launch_bounds__(kThreads2, 1)
     mbar_init(&sm.mma_drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // Longest segments first: the segment whose rank (#segments longer, ties
-  // by index) equals this CTA's order; one thread per candidate segment,
-  // lengths staged in shared memory when they fit.
-  const bool lens_in_smem = a.n_seg <= kMaxSegLens;
-  if (lens_in_smem)
+  // ---- schedule: segment ranks (longest first, ties by index) ----
+  if (S.staged)
     for (int s = threadIdx.x; s < a.n_seg; s += blockDim.x) sm.seg_len[s] = a.cu[s + 1] - a.cu[s];
   __syncthreads();
-  for (int s = threadIdx.x; s < a.n_seg; s += blockDim.x) {
-    const int ls = lens_in_smem ? sm.seg_len[s] : a.cu[s + 1] - a.cu[s];
-    int rank = 0;
-    for (int o = 0; o < a.n_seg; ++o) {
-      const int lo = lens_in_smem ? sm.seg_len[o] : a.cu[o + 1] - a.cu[o];
-      rank += (lo > ls) || (lo == ls && o < s);
+  {
+    const int my_order = b / S.U;  // phase-1 rank of this CTA (unstaged grids)
+    for (int s = threadIdx.x; s < a.n_seg; s += blockDim.x) {
+      const int ls = S.seg_len(s);
+      int rank = 0;
+      for (int o = 0; o < a.n_seg; ++o) {
+        const int lo = S.seg_len(o);
+        rank += (lo > ls) || (lo == ls && o < s);
+      }
+      if (S.staged)
+        sm.order[rank] = int16_t(s);
+      else if (rank == my_order)
+        sm.seg1 = s;
     }
-    if (rank == order) sm.seg = s;
+  }
+  __syncthreads();
+  // ---- schedule: phase-2 cost prefix and CTA ranges (warp 0) ----
+  // Costs are in units of the measured step times: phase-1 steps weigh
+  // w_pair / w_single, phase-2 steps w2_pair / w2_single (a piece's steps run
+  // a little slower there, its K/V less often found in L2), every piece
+  // w_fixed more.  CTA b's phase-2 range is its share of the phase-2 work
+  // that brings it to the mean total cost.
+  if (split && warp == 0) {
+    int seg, u, ntile, nkv;
+    const int per = (S.n2 + 31) / 32;
+    const int i0 = min(S.n2, lane * per), i1 = min(S.n2, i0 + per);
+    int64_t run = 0;
+    for (int i = i0; i < i1; ++i) {
+      S.unit(S.n1 + i, seg, u, ntile, nkv);
+      run += int64_t(nkv) * S.weight(ntile);
+    }
+    int64_t incl = run;  // inclusive warp scan of the lane totals
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    run = incl - run;
+    for (int i = i0; i < i1; ++i) {
+      S.unit(S.n1 + i, seg, u, ntile, nkv);
+      run += int64_t(nkv) * S.weight(ntile);
+      sm.pre2[i + 1] = run;
+    }
+    if (lane == 0) sm.pre2[0] = 0;
+    const int64_t P2 = __shfl_sync(0xffffffffu, incl, 31);
+    // phase-1 cost of this lane's CTAs (a contiguous chunk of <= 5)
+    const int per1 = (S.G + 31) / 32;
+    const int c0 = min(S.G, lane * per1), c1e = min(S.G, c0 + per1);
+    int64_t c1 = 0;
+    for (int i = c0; i < c1e; ++i) {
+      S.unit(i, seg, u, ntile, nkv);
+      c1 += nkv > 0 ? int64_t(nkv) * (ntile == 2 ? a.w_pair : a.w_single) + a.w_fixed : 0;
+    }
+    int64_t c1_all = c1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c1_all += __shfl_xor_sync(0xffffffffu, c1_all, o);
+    const double T = double(c1_all + P2 + int64_t(S.n2) * a.w_fixed) / S.G;
+    double bl = 0.0;  // this lane's budgets: T - phase-1 cost, at least 0
+    for (int i = c0; i < c1e; ++i) {
+      S.unit(i, seg, u, ntile, nkv);
+      const int64_t c = nkv > 0 ? int64_t(nkv) * (ntile == 2 ? a.w_pair : a.w_single) + a.w_fixed : 0;
+      bl += fmax(0.0, T - double(c));
+    }
+    double binc = bl;  // inclusive scan of the lane budget sums
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double y = __shfl_up_sync(0xffffffffu, binc, o);
+      if (lane >= o) binc += y;
+    }
+    const double bsum = __shfl_sync(0xffffffffu, binc, 31);
+    const double scale = bsum > 0.0 ? double(P2) / bsum : 0.0;
+    double acc = binc - bl;
+    for (int i = c0; i < c1e; ++i) {
+      if (bsum > 0.0) {
+        sm.bnd[i] = int64_t(acc * scale);
+        S.unit(i, seg, u, ntile, nkv);
+        const int64_t c =
+            nkv > 0 ? int64_t(nkv) * (ntile == 2 ? a.w_pair : a.w_single) + a.w_fixed : 0;
+        acc += fmax(0.0, T - double(c));
+      } else {
+        sm.bnd[i] = int64_t(double(P2) * (double(i) / S.G));
+      }
+    }
+    if (lane == 0) sm.bnd[S.G] = P2;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -411,247 +665,361 @@ __global__ void __launch_bounds__(kThreads2, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-
-  const int seg = sm.seg;
-  const int unit = sm.unit;
   const uint32_t tmem = sm.tmem_base;
-  const int c = seg >= 0 ? seg / a.H : 0;
-  const int h = seg >= 0 ? seg - c * a.H : 0;
-  const int kv0 = seg >= 0 ? a.cu[seg] : 0;
-  const int lk = seg >= 0 ? a.cu[seg + 1] - kv0 : 0;
-  const int nkv = (lk + kBN - 1) / kBN;
-  const int ntile = (2 * unit + 1 < a.m_tiles) ? 2 : 1;  // query tiles in this CTA
-  const int row0 = c * a.rows_per_chunk + 2 * unit * kBM;  // global query row of tile 0
 
-  if (seg >= 0 && nkv > 0) {
-    if (warp == 0) {
-      // ---------------- TMA producer ----------------
-      if (lane == 0) {
-        mbar_expect_tx(&sm.q_full, ntile * kTileBytes);
-        for (int t = 0; t < ntile; ++t) {
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      Cursor cur{0, 0};
+      Piece p;
+      int pi = 0, gs = 0, q_issued = -1;
+      while (!*abort && next_piece(S, b, cur, p)) {
+        if (pi > 0 && !mbar_wait(&sm.q_empty, (pi - 1) & 1, abort, a.status)) break;
+        const int c = p.seg / a.H, h = p.seg - c * a.H;
+        const int row0 = c * a.rows_per_chunk + 2 * p.unit * kBM;
+        mbar_expect_tx(&sm.q_full, p.ntile * kTileBytes);
+        for (int t = 0; t < p.ntile; ++t) {
           tma_load_3d(sm.q[t], &tm_q, &sm.q_full, 0, h, row0 + t * kBM);
           tma_load_3d(sm.q[t] + kHalfBytes, &tm_q, &sm.q_full, 64, h, row0 + t * kBM);
         }
-        int issued = 0;
-        for (int j = 0; j < nkv; ++j) {
-          const int s = j % kStages2;
-          if (j >= kStages2 &&
-              !mbar_wait(&sm.kv_empty[s], ((j / kStages2) + 1) & 1, abort, a.status))
+        q_issued = pi;
+        bool ok = true;
+        // K/V tiles the ring reaches in the next steps go to L2 now, so their
+        // loads find them there even when no neighbouring CTA read them
+        for (int j = p.k0; j < p.k1 && j < p.k0 + a.prefetch; ++j) {
+          const int y = p.kv0 + j * kBN;
+          tma_prefetch_2d(&tm_k, 0, y);
+          tma_prefetch_2d(&tm_k, 64, y);
+          tma_prefetch_2d(&tm_v, 0, y);
+          tma_prefetch_2d(&tm_v, 64, y);
+        }
+        for (int j = p.k0; j < p.k1; ++j, ++gs) {
+          const int s = gs % kStages2;
+          if (gs >= kStages2 &&
+              !mbar_wait(&sm.kv_empty[s], ((gs / kStages2) + 1) & 1, abort, a.status)) {
+            ok = false;
             break;
+          }
           mbar_expect_tx(&sm.kv_full[s], 2 * kTileBytes);
-          const int y = kv0 + j * kBN;
+          const int y = p.kv0 + j * kBN;
           tma_load_2d(sm.k[s], &tm_k, &sm.kv_full[s], 0, y);
           tma_load_2d(sm.k[s] + kHalfBytes, &tm_k, &sm.kv_full[s], 64, y);
           tma_load_2d(sm.v[s], &tm_v, &sm.kv_full[s], 0, y);
           tma_load_2d(sm.v[s] + kHalfBytes, &tm_v, &sm.kv_full[s], 64, y);
-          issued = j + 1;
+          if (a.prefetch > 0 && j + a.prefetch < p.k1) {
+            const int yp = y + a.prefetch * kBN;
+            tma_prefetch_2d(&tm_k, 0, yp);
+            tma_prefetch_2d(&tm_k, 64, yp);
+            tma_prefetch_2d(&tm_v, 0, yp);
+            tma_prefetch_2d(&tm_v, 64, yp);
+          }
         }
-        if (*abort) {
-          // drain this CTA's own copies before the shared memory goes away
+        if (!ok) break;
+        ++pi;
+      }
+      if (*abort) {
+        // drain this CTA's own copies before the shared memory goes away
+        if (q_issued >= 0) {
           const uint64_t t0 = now_ns();
-          while (!mbar_try(&sm.q_full, 0) && now_ns() - t0 < kTimeoutNs) {
+          while (!mbar_try(&sm.q_full, q_issued & 1) && now_ns() - t0 < kTimeoutNs) {
           }
-          for (int j = issued > kStages2 ? issued - kStages2 : 0; j < issued; ++j) {
-            const uint64_t t1 = now_ns();
-            while (!mbar_try(&sm.kv_full[j % kStages2], (j / kStages2) & 1) &&
-                   now_ns() - t1 < kTimeoutNs) {
-            }
+        }
+        for (int g = gs > kStages2 ? gs - kStages2 : 0; g < gs; ++g) {
+          const uint64_t t1 = now_ns();
+          while (!mbar_try(&sm.kv_full[g % kStages2], (g / kStages2) & 1) &&
+                 now_ns() - t1 < kTimeoutNs) {
           }
         }
       }
-    } else if (warp == 1) {
-      // ---------------- MMA issuer ----------------
-      if (lane == 0) {
-        constexpr uint32_t id_qk = idesc_bf16(false);
-        constexpr uint32_t id_pv = idesc_bf16(true);
-        // Descriptor words computed once: the start-address field (bits 0-13,
-        // address >> 4) of a tile plus a constant offset stays inside the field
-        // (shared memory ends below 256 KB), so each MMA's descriptor is one
-        // add on the low word.  One thread keeps the tensor pipe fed with
-        // 128x128x16 MMAs (64 cycles each) only if little scalar work sits
-        // between them: measured on B200, issue takes 64 cycles per MMA with
-        // precomputed descriptors and 110-260 with per-MMA address arithmetic.
-        const uint64_t dq0 = sdesc_sw128(su32(sm.q[0]), 16, 1024);
-        const uint32_t d_hi = uint32_t(dq0 >> 32);  // SBO and layout bits, the same for all
-        const uint32_t q_lo0 = uint32_t(dq0);
-        const uint32_t q_lo1 = uint32_t(sdesc_sw128(su32(sm.q[1]), 16, 1024));
-        const uint32_t k_lo0 = uint32_t(sdesc_sw128(su32(sm.k[0]), 16, 1024));
-        const uint32_t k_lo1 = uint32_t(sdesc_sw128(su32(sm.k[1]), 16, 1024));
-        const uint32_t v_lo0 = uint32_t(sdesc_sw128(su32(sm.v[0]), kHalfBytes, 1024));
-        const uint32_t v_lo1 = uint32_t(sdesc_sw128(su32(sm.v[1]), kHalfBytes, 1024));
-        static_assert(kStages2 == 2, "descriptor words are kept for two stages");
-        auto desc = [d_hi](uint32_t lo) { return (uint64_t(d_hi) << 32) | lo; };
-        auto issue_qk = [&](int t, int j) {
-          const uint32_t q_lo = t ? q_lo1 : q_lo0;
-          const uint32_t k_lo = (j & 1) ? k_lo1 : k_lo0;
-          const uint32_t d_tm = tmem + t * 128;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t id_qk = idesc_bf16(false);
+      constexpr uint32_t id_pv = idesc_bf16(true);
+      // Descriptor words computed once: the start-address field (bits 0-13,
+      // address >> 4) of a tile plus a constant offset stays inside the field
+      // (shared memory ends below 256 KB), so each MMA's descriptor is one
+      // add on the low word.  One thread keeps the tensor pipe fed with
+      // 128x128x16 MMAs (64 cycles each) only if little scalar work sits
+      // between them: measured on B200, issue takes 64 cycles per MMA with
+      // precomputed descriptors and 110-260 with per-MMA address arithmetic.
+      const uint64_t dq0 = sdesc_sw128(su32(sm.q[0]), 16, 1024);
+      const uint32_t d_hi = uint32_t(dq0 >> 32);  // SBO and layout bits, the same for all
+      const uint32_t q_lo0 = uint32_t(dq0);
+      const uint32_t q_lo1 = uint32_t(sdesc_sw128(su32(sm.q[1]), 16, 1024));
+      const uint32_t k_lo0 = uint32_t(sdesc_sw128(su32(sm.k[0]), 16, 1024));
+      const uint32_t k_lo1 = uint32_t(sdesc_sw128(su32(sm.k[1]), 16, 1024));
+      const uint32_t v_lo0 = uint32_t(sdesc_sw128(su32(sm.v[0]), kHalfBytes, 1024));
+      const uint32_t v_lo1 = uint32_t(sdesc_sw128(su32(sm.v[1]), kHalfBytes, 1024));
+      static_assert(kStages2 == 2, "descriptor words are kept for two stages");
+      auto desc = [d_hi](uint32_t lo) { return (uint64_t(d_hi) << 32) | lo; };
+      auto issue_qk = [&](int t, int g) {
+        const uint32_t q_lo = t ? q_lo1 : q_lo0;
+        const uint32_t k_lo = (g & 1) ? k_lo1 : k_lo0;
+        const uint32_t d_tm = tmem + t * 128;
 #pragma unroll
-          for (int kk = 0; kk < kHD / 16; ++kk) {
-            const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
-            mma_ss(d_tm, desc(q_lo + off), desc(k_lo + off), id_qk, kk > 0 ? 1u : 0u);
-          }
-          tc_commit(&sm.s_full[t]);
-        };
-        auto issue_pv = [&](int t, int j) {
-          const uint32_t v_lo = (j & 1) ? v_lo1 : v_lo0;
-          const uint32_t d_tm = tmem + 256 + t * 128, p_tm = tmem + t * 128;
-          const uint32_t acc0 = j > 0 ? 1u : 0u;
+        for (int kk = 0; kk < kHD / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+          mma_ss(d_tm, desc(q_lo + off), desc(k_lo + off), id_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&sm.s_full[t]);
+      };
+      auto issue_pv = [&](int t, int g, bool first) {
+        const uint32_t v_lo = (g & 1) ? v_lo1 : v_lo0;
+        const uint32_t d_tm = tmem + 256 + t * 128, p_tm = tmem + t * 128;
+        const uint32_t acc0 = first ? 0u : 1u;
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            // A = P_t (TMEM, 2 bf16 per column), B = V rows kk*16.. (MN-major)
-            mma_ts(d_tm, p_tm + kk * 8, desc(v_lo + ((kk * 2048) >> 4)), id_pv,
-                   kk > 0 ? 1u : acc0);
-          }
-        };
-        bool ok = mbar_wait(&sm.q_full, 0, abort, a.status);
-        if (ok) ok = mbar_wait(&sm.kv_full[0], 0, abort, a.status);
-        if (ok) {
-          tc_fence_after();
-          for (int t = 0; t < ntile; ++t) issue_qk(t, 0);
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // A = P_t (TMEM, 2 bf16 per column), B = V rows kk*16.. (MN-major)
+          mma_ts(d_tm, p_tm + kk * 8, desc(v_lo + ((kk * 2048) >> 4)), id_pv,
+                 kk > 0 ? 1u : acc0);
         }
-        for (int j = 0; ok && j < nkv; ++j) {
-          const bool more = j + 1 < nkv;
-          if (!mbar_wait(&sm.p_full[0], j & 1, abort, a.status)) break;
-          tc_fence_after();
-          issue_pv(0, j);
-          if (!more) tc_commit(&sm.o_final[0]);
-          if (more) {
-            const int s1 = (j + 1) % kStages2;
-            if (!mbar_wait(&sm.kv_full[s1], ((j + 1) / kStages2) & 1, abort, a.status)) break;
-            tc_fence_after();
-            issue_qk(0, j + 1);
-          }
-          if (ntile == 2) {
-            if (!mbar_wait(&sm.p_full[1], j & 1, abort, a.status)) break;
-            tc_fence_after();
-            issue_pv(1, j);
-            if (!more) tc_commit(&sm.o_final[1]);
-          }
-          tc_commit(&sm.kv_empty[j % kStages2]);
-          if (ntile == 2 && more) issue_qk(1, j + 1);
-        }
-        // every MMA issued here completes before the CTA frees TMEM
-        tc_commit(&sm.mma_drain);
-        const uint64_t t0 = now_ns();
-        while (!mbar_try(&sm.mma_drain, 0) && now_ns() - t0 < kTimeoutNs) {
-        }
-      }
-    } else {
-      // ---------------- softmax / correction / epilogue of tile t ----------------
-      const int t = (warp - 2) >> 2;
-      if (t < ntile) {
-        const int quad = warp & 3;
-        const int row = quad * 32 + lane;
-        const uint32_t lane_off = uint32_t(quad * 32) << 16;
-        const uint32_t s_tm = tmem + t * 128 + lane_off;
-        const uint32_t o_tm = tmem + 256 + t * 128 + lane_off;
-        const float sc = a.scale_log2;
-        float m_ref = -INFINITY;  // running reference maximum (log2 domain)
-        float l_sum = 0.0f;
-        bool ok = true;
-        for (int j = 0; j < nkv; ++j) {
-          if (!mbar_wait(&sm.s_full[t], j & 1, abort, a.status)) {
+      };
+      Cursor cur{0, 0};
+      Piece p;
+      int pi = 0, gs = 0, ts0 = 0, ts1 = 0;
+      bool ok = true;
+      while (ok && next_piece(S, b, cur, p)) {
+        const int n = p.k1 - p.k0;
+        ok = mbar_wait(&sm.q_full, pi & 1, abort, a.status);
+        if (ok) ok = mbar_wait(&sm.kv_full[gs % kStages2], (gs / kStages2) & 1, abort, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        for (int t = 0; t < p.ntile; ++t) issue_qk(t, gs);
+        for (int j = 0; j < n; ++j) {
+          const int g = gs + j;
+          const bool more = j + 1 < n;
+          if (!mbar_wait(&sm.p_full[0], (ts0 + j) & 1, abort, a.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint32_t sr[4][32];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) tmem_ld32(s_tm + q * 32, sr[q]);
-          tmem_wait_ld();
-          const int valid = lk - j * kBN;  // keys of this tile inside the segment
-          const bool partial = valid < kBN;
-          if (partial) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                if (q * 32 + e >= valid) sr[q][e] = __float_as_uint(-INFINITY);
-          }
-          const float m_new = fmaxf(m_ref, row_max128(sr) * sc);
-          const bool grow = m_new > m_ref + kRescaleThreshold || j == 0;
-          float alpha = 1.0f;
-          if (grow) {
-            alpha = (j == 0) ? 0.0f : fast_exp2(m_ref - m_new);
-            m_ref = m_new;
-          }
-          const f2 scale2 = mk2(sc, sc), negm2 = mk2(-m_ref, -m_ref);
-          f2 acc[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = mk2(0.0f, 0.0f);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t pr[16];
-            if (partial)
-              softmax_chunk<false>(sr[q], scale2, negm2, acc[2 * q], acc[2 * q + 1], pr);
-            else
-              softmax_chunk<true>(sr[q], scale2, negm2, acc[2 * q], acc[2 * q + 1], pr);
-            tmem_st16(s_tm + q * 16, pr);
-          }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc[i] = add2(acc[i], acc[i + 4]);
-          acc[0] = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
-          float r0, r1;
-          un2(acc[0], r0, r1);
-          l_sum = l_sum * alpha + (r0 + r1);
-          // O_t *= alpha for the rows whose reference maximum moved.  S_t(j)
-          // was committed after PV_t(j-1), so O_t is complete here.
-          if (j > 0 && __any_sync(0xffffffffu, grow)) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t orr[32];
-              tmem_ld32(o_tm + q * 32, orr);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-              tmem_st32(o_tm + q * 32, orr);
+          issue_pv(0, g, j == 0);
+          if (!more) tc_commit(&sm.o_final[0]);
+          if (more) {
+            if (!mbar_wait(&sm.kv_full[(g + 1) % kStages2], ((g + 1) / kStages2) & 1, abort,
+                           a.status)) {
+              ok = false;
+              break;
             }
+            tc_fence_after();
+            issue_qk(0, g + 1);
           }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.p_full[t]);
+          if (p.ntile == 2) {
+            if (!mbar_wait(&sm.p_full[1], (ts1 + j) & 1, abort, a.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(1, g, j == 0);
+            if (!more) tc_commit(&sm.o_final[1]);
+          }
+          tc_commit(&sm.kv_empty[g % kStages2]);
+          if (p.ntile == 2 && more) issue_qk(1, g + 1);
         }
-        if (ok && mbar_wait(&sm.o_final[t], 0, abort, a.status)) {
-          tc_fence_after();
-          const int grow_row = (2 * unit + t) * kBM + row;
-          const bool store = grow_row < a.rows_per_chunk;
-          const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
-          uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + grow_row) * a.o_row_stride +
-                          int64_t(h) * a.o_head_stride;
+        if (!ok) break;
+        tc_commit(&sm.q_empty);  // every Q·K^T of this piece has been issued
+        gs += n;
+        ts0 += n;
+        if (p.ntile == 2) ts1 += n;
+        ++pi;
+      }
+      // every MMA issued here completes before the CTA frees TMEM
+      tc_commit(&sm.mma_drain);
+      const uint64_t t0 = now_ns();
+      while (!mbar_try(&sm.mma_drain, 0) && now_ns() - t0 < kTimeoutNs) {
+      }
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue of tile t ----------------
+    const int t = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = uint32_t(quad * 32) << 16;
+    const uint32_t s_tm = tmem + t * 128 + lane_off;
+    const uint32_t o_tm = tmem + 256 + t * 128 + lane_off;
+    const float sc = a.scale_log2;
+    // empty segments: zero their output rows (segments b, b + G, ...)
+    for (int s = b; s < a.n_seg; s += S.G) {
+      if (S.seg_len(s) != 0) continue;
+      const int c = s / a.H, h = s - c * a.H;
+      for (int r = threadIdx.x - 64; r < a.rows_per_chunk; r += kThreads2 - 64) {
+        uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + r) * a.o_row_stride +
+                        int64_t(h) * a.o_head_stride;
+        for (int e = 0; e < kHD; e += 8)
+          *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    Cursor cur{0, 0};
+    Piece p;
+    int ts = 0, tp = 0, slots = 0;
+    bool ok = true;
+    while (ok && next_piece(S, b, cur, p)) {
+      if (t >= p.ntile) continue;
+      const int n = p.k1 - p.k0;
+      float m_ref = -INFINITY;  // running reference maximum (log2 domain)
+      float l_sum = 0.0f;
+      for (int j = 0; j < n; ++j) {
+        if (!mbar_wait(&sm.s_full[t], (ts + j) & 1, abort, a.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld32(s_tm + q * 32, sr[q]);
+        tmem_wait_ld();
+        const int valid = p.lk - (p.k0 + j) * kBN;  // keys of this tile inside the segment
+        const bool partial = valid < kBN;
+        if (partial) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (q * 32 + e >= valid) sr[q][e] = __float_as_uint(-INFINITY);
+        }
+        const float m_new = fmaxf(m_ref, row_max128(sr) * sc);
+        const bool grow = m_new > m_ref + kRescaleThreshold || j == 0;
+        float alpha = 1.0f;
+        if (grow) {
+          alpha = (j == 0) ? 0.0f : fast_exp2(m_ref - m_new);
+          m_ref = m_new;
+        }
+        const f2 scale2 = mk2(sc, sc), negm2 = mk2(-m_ref, -m_ref);
+        f2 acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = mk2(0.0f, 0.0f);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pr[16];
+          if (partial)
+            softmax_chunk<false>(sr[q], scale2, negm2, acc[2 * q], acc[2 * q + 1], pr);
+          else
+            softmax_chunk<true>(sr[q], scale2, negm2, acc[2 * q], acc[2 * q + 1], pr);
+          tmem_st16(s_tm + q * 16, pr);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] = add2(acc[i], acc[i + 4]);
+        acc[0] = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+        float r0, r1;
+        un2(acc[0], r0, r1);
+        l_sum = l_sum * alpha + (r0 + r1);
+        // O_t *= alpha for the rows whose reference maximum moved.  S_t(j)
+        // was committed after PV_t(j-1), so O_t is complete here.
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t orr[32];
             tmem_ld32(o_tm + q * 32, orr);
             tmem_wait_ld();
-            if (store) {
 #pragma unroll
-              for (int e = 0; e < 32; e += 8) {
-                uint4 w;
-                w.x = pack_bf16x2(__uint_as_float(orr[e + 0]) * inv,
-                                  __uint_as_float(orr[e + 1]) * inv);
-                w.y = pack_bf16x2(__uint_as_float(orr[e + 2]) * inv,
-                                  __uint_as_float(orr[e + 3]) * inv);
-                w.z = pack_bf16x2(__uint_as_float(orr[e + 4]) * inv,
-                                  __uint_as_float(orr[e + 5]) * inv);
-                w.w = pack_bf16x2(__uint_as_float(orr[e + 6]) * inv,
-                                  __uint_as_float(orr[e + 7]) * inv);
-                *reinterpret_cast<uint4*>(dst + q * 32 + e) = w;
-              }
-            }
+            for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+            tmem_st32(o_tm + q * 32, orr);
           }
         }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[t]);
       }
-    }
-  } else if (seg >= 0 && warp >= 2) {
-    // empty segment: zero this CTA's output rows
-    const int t = (warp - 2) >> 2;
-    const int grow_row = (2 * unit + t) * kBM + (warp & 3) * 32 + lane;
-    if (t < ntile && grow_row < a.rows_per_chunk) {
+      if (!ok || !mbar_wait(&sm.o_final[t], tp & 1, abort, a.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      ts += n;
+      ++tp;
+      const int c = p.seg / a.H, h = p.seg - c * a.H;
+      const int grow_row = (2 * p.unit + t) * kBM + row;
+      const bool store = grow_row < a.rows_per_chunk;
       uint16_t* dst = a.out + int64_t(c * a.rows_per_chunk + grow_row) * a.o_row_stride +
                       int64_t(h) * a.o_head_stride;
-      for (int e = 0; e < kHD; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
+      if (p.whole) {
+        const float inv = l_sum > 0.0f ? 1.0f / l_sum : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t orr[32];
+          tmem_ld32(o_tm + q * 32, orr);
+          tmem_wait_ld();
+          if (store) store_row32(dst + q * 32, orr, inv);
+        }
+        continue;
+      }
+      // ---- a piece of a split unit: partial out, last arrival combines ----
+      if (slots >= 2) {  // cannot happen: only a range's first and last pieces split
+        flag(a.status, PKV_ST_SLOT_RANGE);
+        continue;
+      }
+      float* mine = part_block(a, b, slots++, t);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t orr[32];
+        tmem_ld32(o_tm + q * 32, orr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mine[(q * 32 + e) * kBM + row] = __uint_as_float(orr[e]);
+      }
+      mine[128 * kBM + row] = m_ref;
+      mine[129 * kBM + row] = l_sum;
+      if (lane == 0) reinterpret_cast<int*>(mine + 130 * kBM)[quad] = p.q;
+      __threadfence();
+      __syncwarp();
+      const int q2 = p.q - S.n1;
+      const int w = S.weight(p.ntile);
+      const int nkv = (p.lk + kBN - 1) / kBN;
+      const int64_t u_lo = sm.pre2[q2], u_hi = sm.pre2[q2 + 1];
+      const int j_lo = S.cta_at(u_lo);
+      int last = 0;
+      if (lane == 0) {
+        int npieces = 0;
+        for (int j = j_lo; j < S.G && sm.bnd[j] < u_hi; ++j)
+          npieces += S.cut(sm.bnd[j + 1], q2, w, nkv) > S.cut(sm.bnd[j], q2, w, nkv);
+        int* ctr = a.cnt + (size_t(p.q) * 2 + t) * 4 + quad;
+        const int old = atomicAdd(ctr, 1);
+        last = old == npieces - 1;
+        if (last) *ctr = 0;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence();
+      // combine every piece's rows (this one's included, from the workspace)
+      float M = -INFINITY;
+      for (int j = j_lo; j < S.G && sm.bnd[j] < u_hi; ++j) {
+        if (S.cut(sm.bnd[j + 1], q2, w, nkv) <= S.cut(sm.bnd[j], q2, w, nkv)) continue;
+        const float* pj = part_block(a, j, 0, t);
+        if (__ldcg(reinterpret_cast<const int*>(pj + 130 * kBM) + quad) != p.q)
+          pj = part_block(a, j, 1, t);
+        M = fmaxf(M, __ldcg(pj + 128 * kBM + row));
+      }
+      float L = 0.0f;
+      for (int j = j_lo; j < S.G && sm.bnd[j] < u_hi; ++j) {
+        if (S.cut(sm.bnd[j + 1], q2, w, nkv) <= S.cut(sm.bnd[j], q2, w, nkv)) continue;
+        const float* pj = part_block(a, j, 0, t);
+        if (__ldcg(reinterpret_cast<const int*>(pj + 130 * kBM) + quad) != p.q)
+          pj = part_block(a, j, 1, t);
+        L += fast_exp2(__ldcg(pj + 128 * kBM + row) - M) * __ldcg(pj + 129 * kBM + row);
+      }
+      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        float accv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) accv[e] = 0.0f;
+        for (int j = j_lo; j < S.G && sm.bnd[j] < u_hi; ++j) {
+          if (S.cut(sm.bnd[j + 1], q2, w, nkv) <= S.cut(sm.bnd[j], q2, w, nkv)) continue;
+          const float* pj = part_block(a, j, 0, t);
+          if (__ldcg(reinterpret_cast<const int*>(pj + 130 * kBM) + quad) != p.q)
+            pj = part_block(a, j, 1, t);
+          const float wj = fast_exp2(__ldcg(pj + 128 * kBM + row) - M);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) accv[e] = fmaf(wj, __ldcg(pj + (q * 32 + e) * kBM + row), accv[e]);
+        }
+        uint32_t ob[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ob[e] = __float_as_uint(accv[e]);
+        if (store) store_row32(dst + q * 32, ob, inv);
+      }
     }
   }
 
@@ -759,10 +1127,43 @@ static bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_
   return r == CUDA_SUCCESS;
 }
 
+// Cost weights of the schedule: a phase-1 K/V step of a tile pair and of a
+// lone tile, the fixed cost of one piece, a phase-2 step of a pair and of a
+// lone tile; and how many K/V steps ahead the producer pulls tiles into L2
+// (0: none; measured no gain).  PKV_ATTN_COST="p1,s1,fixed,p2,s2" and
+// PKV_ATTN_PREFETCH=steps override them (tuning).
+static void attn_weights(AttnArgs& a) {
+  static int w[6] = {0, 0, 0, 0, 0, 0};
+  static std::once_flag once;
+  std::call_once(once, [] {
+    // measured on B200 (C2 attend shape): a lone-tile step takes 0.89 of a
+    // pair step, phase-2 steps ~1.08 of phase-1 ones, a piece ~1.3 steps more
+    const int def[6] = {9, 8, 12, 10, 9, 0};
+    for (int i = 0; i < 6; ++i) w[i] = def[i];
+    if (const char* e = getenv("PKV_ATTN_COST")) {
+      int v[5] = {0, 0, 0, 0, 0};
+      if (sscanf(e, "%d,%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3], &v[4]) == 5 && v[0] > 0 &&
+          v[1] > 0 && v[2] >= 0 && v[3] > 0 && v[4] > 0)
+        for (int i = 0; i < 5; ++i) w[i] = v[i];
+    }
+    if (const char* e = getenv("PKV_ATTN_PREFETCH")) {
+      const int d = atoi(e);
+      if (d >= 0 && d <= 8) w[5] = d;
+    }
+  });
+  a.w_pair = w[0];
+  a.w_single = w[1];
+  a.w_fixed = w[2];
+  a.w2_pair = w[3];
+  a.w2_single = w[4];
+  a.prefetch = w[5];
+}
+
 int launch_attention(const uint16_t* q, int64_t q_rs, int64_t q_hs, const uint16_t* k,
                      const uint16_t* v, int64_t kv_rows, const int32_t* cu, int num_chunks,
                      int H, int rows_per_chunk, int D, float scale, uint16_t* out, int64_t o_rs,
-                     int64_t o_hs, int32_t* status, cudaStream_t stream) {
+                     int64_t o_hs, int32_t* status, const AttnWorkspace* ws,
+                     cudaStream_t stream) {
   if (num_chunks == 0 || H == 0 || rows_per_chunk == 0) return PKV_OK;
   if (!q || !k || !v || !cu || !out || num_chunks < 0 || H < 0 || rows_per_chunk < 0 || D <= 0)
     return PKV_EINVAL;
@@ -797,16 +1198,33 @@ int launch_attention(const uint16_t* q, int64_t q_rs, int64_t q_hs, const uint16
       a.o_row_stride = o_rs;
       a.o_head_stride = o_hs;
       a.status = status;
+      attn_weights(a);
       const size_t smem = sizeof(AttnSmem2) + 1024;
-      static bool attr_set = false;
-      if (!attr_set) {
-        if (cudaFuncSetAttribute(attn_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 int(smem)) != cudaSuccess)
-          return PKV_ELAUNCH;
-        attr_set = true;
+      static std::mutex mu;
+      static int attr_done[kMaxDevices] = {};
+      if (per_device_once(attr_done, mu, [smem] {
+            return cudaFuncSetAttribute(attn_tc2_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(smem)) == cudaSuccess
+                       ? 1
+                       : 0;
+          }) <= 0) {
+        cudaGetLastError();
+        return PKV_ELAUNCH;
       }
-      const int units = (a.m_tiles + 1) / 2;
-      attn_tc2_kernel<<<n_seg * units, kThreads2, smem, stream>>>(mq, mk, mv, a);
+      const int64_t units = int64_t(n_seg) * ((a.m_tiles + 1) / 2);
+      // persistent stream-K grid when a workspace is given and the units
+      // outnumber the SMs (the schedule's arrays fit shared memory)
+      int grid = int(units);
+      const int G = sm_count() < kMaxCtas ? sm_count() : kMaxCtas;
+      if (ws != nullptr && ws->part != nullptr && ws->cnt != nullptr && units > G &&
+          units <= ws->cnt_units && n_seg <= kMaxSegLens && units - G <= kMaxSplitUnits) {
+        a.part = ws->part;
+        a.cnt = ws->cnt;
+        grid = G;
+      }
+      if (units >= (int64_t(1) << 31)) return PKV_EUNSUPPORTED;
+      attn_tc2_kernel<<<grid, kThreads2, smem, stream>>>(mq, mk, mv, a);
       return launch_status();
     }
   }
@@ -828,7 +1246,40 @@ extern "C" int pkv_attention(const uint16_t* q, int64_t q_row_stride, int64_t q_
                              int64_t o_row_stride, int64_t o_head_stride, pkv_stream_t stream) {
   return launch_attention(q, q_row_stride, q_head_stride, k, v, kv_rows, cu_seqlens_k,
                           num_chunks, num_heads, rows_per_chunk, head_dim, softmax_scale, out,
-                          o_row_stride, o_head_stride, nullptr, static_cast<cudaStream_t>(stream));
+                          o_row_stride, o_head_stride, nullptr, nullptr,
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t pkv_attention_workspace_bytes(int num_chunks, int num_heads,
+                                                 int rows_per_chunk) {
+  if (num_chunks < 0 || num_heads < 0 || rows_per_chunk < 0) return 0;
+  const int64_t tiles = (int64_t(rows_per_chunk) + kBM - 1) / kBM;
+  const int64_t units = int64_t(num_chunks) * num_heads * ((tiles + 1) / 2);
+  return align256(kAttnPartBytes) + align256(units * kAttnCntPerUnit * 4);
+}
+
+extern "C" int pkv_attention_ws(const uint16_t* q, int64_t q_row_stride, int64_t q_head_stride,
+                                const uint16_t* k, const uint16_t* v, int64_t kv_rows,
+                                const int32_t* cu_seqlens_k, int num_chunks, int num_heads,
+                                int rows_per_chunk, int head_dim, float softmax_scale,
+                                uint16_t* out, int64_t o_row_stride, int64_t o_head_stride,
+                                void* workspace, int64_t workspace_bytes, pkv_stream_t stream) {
+  if (workspace == nullptr)
+    return pkv_attention(q, q_row_stride, q_head_stride, k, v, kv_rows, cu_seqlens_k,
+                         num_chunks, num_heads, rows_per_chunk, head_dim, softmax_scale, out,
+                         o_row_stride, o_head_stride, stream);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0 ||
+      workspace_bytes < pkv_attention_workspace_bytes(num_chunks, num_heads, rows_per_chunk))
+    return PKV_EINVAL;
+  AttnWorkspace ws{};
+  char* base = static_cast<char*>(workspace);
+  ws.part = reinterpret_cast<float*>(base);
+  ws.cnt = reinterpret_cast<int32_t*>(base + align256(kAttnPartBytes));
+  ws.cnt_units = (workspace_bytes - align256(kAttnPartBytes)) / (kAttnCntPerUnit * 4);
+  return launch_attention(q, q_row_stride, q_head_stride, k, v, kv_rows, cu_seqlens_k,
+                          num_chunks, num_heads, rows_per_chunk, head_dim, softmax_scale, out,
+                          o_row_stride, o_head_stride, nullptr, &ws,
+                          static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pkv_wait_selftest(int32_t* status, int64_t limit_ns, int32_t* result,

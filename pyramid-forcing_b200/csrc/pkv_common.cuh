@@ -10,6 +10,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -103,15 +104,35 @@ inline int launch_status() {
   return e == cudaSuccess ? PKV_OK : PKV_ELAUNCH;
 }
 
+constexpr int kMaxDevices = 64;
+
+// A positive value computed once per device, on the first call made with
+// that device current (a kernel's shared-memory opt-in, a device attribute).
+// Host threads may call concurrently; fn() returning <= 0 is not cached.
+template <typename Fn>
+inline int per_device_once(int (&cache)[kMaxDevices], std::mutex& mu, Fn fn) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return fn();
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] > 0) return cache[dev];
+  const int v = fn();
+  if (v > 0) cache[dev] = v;
+  return v;
+}
+
+// Streaming multiprocessors of the current device.
 inline int sm_count() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
+  static std::mutex mu;
+  static int cache[kMaxDevices] = {};
+  return per_device_once(cache, mu, [] {
+    int dev = 0, n = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
+    return n > 0 ? n : 148;
+  });
 }
 
 // Scratch arena layout used by the fused update / attend paths.  Offsets are
@@ -122,10 +143,26 @@ struct ScratchLayout {
   int64_t copy_items;  // fused-update copy work list
   int64_t plan;        // cu + sk/sg/sl/dst + traw/tremap for max_attend_chunks
   int64_t plan_total;  // int64 packed-token total of the last plan
+  int64_t attn_part;   // attention: per-CTA partial results of split units
+  int64_t attn_cnt;    // attention: per-(unit, tile, warp) arrival counters
   int64_t bytes;
 };
 
 constexpr int kMaxFramesPerUpdate = 16;
+
+// Ragged-attention workspace (pkv_attn.cu): per persistent CTA two slots x
+// two query tiles of fp32 partials (130 rows of 128: O columns, m, l, plus 32
+// words of headers), and an arrival counter per (unit, tile, warp).
+constexpr int kAttnMaxCtas = 160;
+constexpr int64_t kAttnPartFloats = 130 * 128 + 32;
+constexpr int64_t kAttnPartBytes = int64_t(kAttnMaxCtas) * 4 * kAttnPartFloats * 4;
+constexpr int kAttnCntPerUnit = 8;
+
+// Attention units (segment x pair of 128-row query tiles) of the largest attend.
+inline int64_t attn_units(const pkv_cache_t* c) {
+  const int64_t tiles = (int64_t(c->frame_seqlen) + 127) / 128;
+  return int64_t(c->max_attend_chunks) * c->num_heads * ((tiles + 1) / 2);
+}
 
 inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
@@ -149,6 +186,10 @@ inline ScratchLayout scratch_layout(const pkv_cache_t* c) {
   off = align256(off + N * 4 * 4 + 8 + N * 8 * 2);
   s.plan_total = off;
   off = align256(off + 64);
+  s.attn_part = off;
+  off = align256(off + kAttnPartBytes);
+  s.attn_cnt = off;
+  off = align256(off + attn_units(c) * kAttnCntPerUnit * 4);
   s.bytes = off;
   return s;
 }

@@ -49,9 +49,19 @@ int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, cons
                 int ft_rows, int ft_cols, const float* fy, int fy_rows, int fy_cols,
                 const float* fx, int fx_rows, int fx_cols, cudaStream_t stream);
 
+// Ragged-attention workspace: partial-result slots and arrival counters for
+// `cnt_units` units (zeroed before the first launch; each launch leaves them
+// zero).  nullptr: one CTA per unit, nothing split.
+struct AttnWorkspace {
+  float* part;
+  int32_t* cnt;
+  int64_t cnt_units;
+};
+
 int launch_attention(const uint16_t* q, int64_t q_rs, int64_t q_hs, const uint16_t* k,
                      const uint16_t* v, int64_t kv_rows, const int32_t* cu, int num_chunks,
                      int H, int rows_per_chunk, int D, float scale, uint16_t* out, int64_t o_rs,
-                     int64_t o_hs, int32_t* status, cudaStream_t stream);
+                     int64_t o_hs, int32_t* status, const AttnWorkspace* ws,
+                     cudaStream_t stream);
 
 }  // namespace pkv

@@ -504,16 +504,21 @@ int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, cons
         reinterpret_cast<uintptr_t>(a.pos[2]) | reinterpret_cast<uintptr_t>(a.pos[3])) % 16 == 0);
   if (bulk_ok) {
     // a persistent grid of exactly the resident blocks
-    static int per_sm = 0;
+    static std::mutex mu;
+    static int per_sm_cache[kMaxDevices] = {};
     const int smem = int(sizeof(BulkSmem)) + 128;
-    if (per_sm == 0) {
+    const int per_sm = per_device_once(per_sm_cache, mu, [smem] {
+      int n = 0;
       if (cudaFuncSetAttribute(pack_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                smem) != cudaSuccess ||
-          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pack_bulk_kernel, kBulkThreads, smem) !=
-              cudaSuccess)
-        return PKV_ELAUNCH;
-      if (per_sm < 1) per_sm = 1;
-    }
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pack_bulk_kernel, kBulkThreads,
+                                                        smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+      }
+      return n < 1 ? 1 : n;
+    });
+    if (per_sm <= 0) return PKV_ELAUNCH;
     pack_bulk_kernel<<<sm_count() * per_sm, kBulkThreads, smem, stream>>>(a);
   } else if (vec) {
     pack_kernel<true><<<int(grid), 256, 0, stream>>>(a);

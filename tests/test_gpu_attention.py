@@ -109,3 +109,64 @@ def test_attention_strided_q_layout(cuda):
     qv = wide[:, 1:H + 1]
     out = _ops.ops().pkv_attention(qv, k, v, cu, C, Lq, D ** -0.5)
     _check(out, _reference(q, k, v, cu, C, H, Lq, D ** -0.5))
+
+
+def _ws(cuda, C, H, Lq):
+    from pyramidkv import _ops
+    n = int(_ops.ops().pkv_attention_ws_bytes(C, H, Lq))
+    return torch.zeros(n, dtype=torch.uint8, device=cuda)
+
+
+def _ws_counters(ws):
+    """The workspace's arrival counters (after the 256-aligned partial slots)."""
+    part = 160 * 4 * (130 * 128 + 32) * 4
+    return ws[(part + 255) // 256 * 256:].view(torch.int32)
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_balanced_attention_c2_shape(cuda, seed):
+    """The SM-balanced (persistent, split-unit) path at the C2 attend shape:
+    3 chunks x 12 heads x 1560 queries over 4-19 frames of keys plus merge
+    anchors, i.e. 252 units on the SMs, so units are cut between SMs and
+    recombined.  Within tolerance of fp32; the workspace's counters are back
+    at zero after every launch, and a second launch is bit-identical."""
+    from pyramidkv import _ops
+    C, H, Lq, D = 3, 12, 1560, 128
+    g = torch.Generator().manual_seed(100 + seed)
+    frames = torch.randint(4, 20, (C * H,), generator=g)
+    lens = (frames * 1560 + (torch.rand(C * H, generator=g) < 0.3).long() * 390).tolist()
+    q, k, v, cu = _case(cuda, C, H, Lq, D, lens, seed=seed)
+    ws = _ws(cuda, C, H, Lq)
+    scale = D ** -0.5
+    out = _ops.ops().pkv_attention_ws(q, k, v, cu, C, Lq, scale, ws)
+    torch.cuda.synchronize()
+    assert int(_ws_counters(ws).abs().sum()) == 0
+    _check(out, _reference(q, k, v, cu, C, H, Lq, scale))
+    again = _ops.ops().pkv_attention_ws(q, k, v, cu, C, Lq, scale, ws)
+    assert torch.equal(again.view(torch.int16), out.view(torch.int16))
+    plain = _ops.ops().pkv_attention(q, k, v, cu, C, Lq, scale)
+    err = (plain.float() - out.float()).abs()
+    assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS
+
+
+def test_balanced_attention_ragged_edges(cuda):
+    """Split path with empty segments, one-key segments, lengths one off a
+    128-key tile, very long and very short segments side by side, and a
+    query count whose last tile has 1 row (so units hold one tile)."""
+    from pyramidkv import _ops
+    C, H, Lq, D = 2, 40, 257, 128            # 3 tiles: one pair + a lone 1-row tile
+    g = torch.Generator().manual_seed(5)
+    choices = [0, 1, 127, 128, 129, 390, 4000, 30000]
+    lens = [choices[int(i)] for i in torch.randint(0, len(choices), (C * H,), generator=g)]
+    lens[0], lens[1] = 60000, 0
+    q, k, v, cu = _case(cuda, C, H, Lq, D, lens, seed=9)
+    ws = _ws(cuda, C, H, Lq)
+    out = _ops.ops().pkv_attention_ws(q, k, v, cu, C, Lq, 0.088, ws)
+    torch.cuda.synchronize()
+    assert int(_ws_counters(ws).abs().sum()) == 0
+    ref = _reference(q, k, v, cu, C, H, Lq, 0.088)
+    _check(out, ref)
+    empty = [i for i, n in enumerate(lens) if n == 0]
+    for i in empty:
+        c, h = divmod(i, H)
+        assert out[c * Lq:(c + 1) * Lq, h].abs().max().item() == 0.0

@@ -5,13 +5,16 @@ runtime that owns the device's memory pool and lends the library only the
 cache and each call's inputs and outputs, or a serving loop where a cudaMalloc
 could synchronise the device.  ``pkv_attend_noalloc`` serves them, with the
 planner's scratch in a fixed device array inside libpkv.so.  This test builds a
-cache through the normal API, then on two calls in a row (layer 0, then layer
-1) compares the allocation-free entry point -- called with ctypes and a cache
-descriptor that has no scratch buffer -- with the existing attend path, within
-the attention tolerance used by the other GPU tests (max abs 2e-2, mean abs
-2e-3).  It also checks that a plan larger than the fixed array is refused
-before anything launches.  The file sorts last, so a run that stops at the
-first failure has already run every other test.
+cache through the normal API, then on consecutive calls (layer 0 and layer 1
+over three chunks, then layer 0 over one chunk, so a smaller plan follows a
+larger one in the shared array) compares the allocation-free entry point --
+called with ctypes and a cache descriptor that has no scratch buffer -- with
+the existing attend path.  At these sizes (at most 12 attention units, fewer
+than the SMs) both run the same plan, pack and one-CTA-per-unit attention, so
+cu_seqlens_k, the packed K/V/positions and the output must be bit-identical.
+It also checks that a plan larger than the fixed array is refused before
+anything launches.  The file sorts last, so a run that stops at the first
+failure has already run every other test.
 """
 from __future__ import annotations
 
@@ -111,23 +114,33 @@ def test_attend_noalloc_matches_attend_on_consecutive_calls(cuda):
     desc = _describe(ctx)
     stream = torch.cuda.current_stream().cuda_stream
     start = 7 * F * FSEQ
-    for call, layer in enumerate((0, 1)):
-        q = rnd()
+    mgr = ctx.mgr
+    for call, (layer, chunks) in enumerate(((0, F), (1, F), (0, 1))):
+        q = rnd()[:, :chunks * FSEQ]
         want = caches[layer].attend(q, start)      # existing entry point (allocating path)
         torch.cuda.synchronize()
+        cu_want = mgr.cu_seqlens_k()[:chunks * H + 1].clone()
+        total = int(cu_want[-1])
+        packed_want = [t[:total].clone() for t in (mgr.k_flat_out(), mgr.v_flat_out(),
+                                                   mgr.pos_flat_out())]
+        for t in (mgr.k_flat_out(), mgr.v_flat_out(), mgr.pos_flat_out(), mgr.cu_seqlens_k()):
+            t.zero_()                               # the entry point must rewrite them
         ft, fy, fx = ctx.freq_parts_flat
         got = torch.empty_like(q)
         rc = lib.pkv_attend_noalloc(
             ctypes.byref(desc), caches[layer].states_bytes_for_layer.data_ptr(), layer,
-            q.data_ptr(), q.stride(1), q.stride(2), F, start // FSEQ, 1,
+            q.data_ptr(), q.stride(1), q.stride(2), chunks, start // FSEQ, 1,
             ctx.sink_time_clamp_min, ctx.sink_time_clamp_max, ctx.decoupled_sink_time_lag,
             ft.data_ptr(), ft.shape[0], ft.shape[1] // 2, fy.data_ptr(), fy.shape[0],
             fy.shape[1] // 2, fx.data_ptr(), fx.shape[0], fx.shape[1] // 2, D ** -0.5,
             got.data_ptr(), got.stride(1), got.stride(2), None, stream)
         assert rc == 0, f"call {call}: rc={rc}"
         torch.cuda.synchronize()
-        err = (got.float() - want.float()).abs()
-        assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, (call, err.max().item())
+        assert torch.equal(mgr.cu_seqlens_k()[:chunks * H + 1], cu_want), call
+        for name, t, w in zip(("k", "v", "pos"), (mgr.k_flat_out(), mgr.v_flat_out(),
+                                                   mgr.pos_flat_out()), packed_want):
+            assert torch.equal(t[:total], w), (call, name)
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), call
     assert ctx.check_status() == 0
 
 
