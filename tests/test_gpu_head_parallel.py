@@ -1,12 +1,14 @@
-"""Head-parallel cache path on 2 GPUs (NCCL), against one GPU.
+"""Head-parallel cache path on 2 and 4 GPUs (NCCL), against one GPU.
 
-Two spawned ranks (one per GPU) each own 2 of the 4 heads of a small model
-and feed ``HeadParallelMegaCache`` their token shard of every block; rank 0
-also runs the single-GPU MegaCache over all heads on the same inputs.  The
-gathered outputs of the ranks must equal the single-GPU outputs bit for bit.
-Skipped with fewer than 2 GPUs.  NVLS is off (NCCL_NVLS_ENABLE=0) and the
-process group has a short timeout, so a failing rank ends the test with an
-error instead of a wait.
+Spawned ranks (one per GPU) each own 4/n of the 4 heads of a small model and
+feed ``HeadParallelMegaCache`` their token shard of every block, through the
+reference's two calls (``update`` then ``attend``: K and V in one exchange, Q
+in another) or through ``step`` (Q, K and V in one exchange).  The single-GPU
+MegaCache over all heads runs on the same inputs; the gathered outputs of the
+ranks must equal it bit for bit (these shapes give every rank the same
+one-CTA-per-unit attention schedule as the single GPU).  Skipped with fewer
+GPUs than ranks.  NVLS is off (NCCL_NVLS_ENABLE=0) and the process group has a
+short timeout, so a failing rank ends the test with an error instead of a wait.
 """
 from __future__ import annotations
 
@@ -23,7 +25,6 @@ import torch.multiprocessing as mp
 from oracle import pkv_oracle as O
 
 pytestmark = pytest.mark.gpu
-WORLD = 2
 L, H, D, W, HG, F = 2, 4, 128, 13, 8, 3
 FSEQ = W * HG
 BLOCKS = 4
@@ -56,24 +57,29 @@ def _inputs():
     return [[(mk(), mk(), mk()) for _ in range(L)] for _ in range(BLOCKS)]
 
 
-def _worker(rank: int, port: int, out_dir: str) -> None:
+def _worker(rank: int, world: int, port: int, out_dir: str, batched: bool) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = f"cuda:{rank}"
-    dist.init_process_group("nccl", rank=rank, world_size=WORLD,
-                            timeout=datetime.timedelta(seconds=60))
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
     try:
         from pyramidkv import head_parallel as hp
         caches = _build(H, _labels(), dev, builder=hp.build_head_parallel_caches)
-        t0, t1 = hp.token_range(rank, WORLD, F * FSEQ)
+        t0, t1 = hp.token_range(rank, world, F * FSEQ)
         got = []
         for blk, layers in enumerate(_inputs()):
             start = blk * F * FSEQ
             for mode in ("noisy", "clean"):
                 for layer, (k, v, q) in enumerate(layers):
                     sh = lambda x: x[:, t0:t1].contiguous().to(dev)  # noqa: E731
-                    caches[layer].update(sh(k), sh(v), start, cache_update_mode=mode)
-                    got.append(caches[layer].attend(sh(q), start).cpu())
+                    if batched:
+                        got.append(caches[layer].step(sh(q), sh(k), sh(v), start,
+                                                      cache_update_mode=mode).cpu())
+                    else:
+                        caches[layer].update(sh(k), sh(v), start, cache_update_mode=mode)
+                        got.append(caches[layer].attend(sh(q), start).cpu())
         torch.cuda.synchronize()
         torch.save(got, os.path.join(out_dir, f"rank{rank}.pt"))
         dist.barrier()
@@ -81,9 +87,11 @@ def _worker(rank: int, port: int, out_dir: str) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_head_parallel_two_gpus_matches_one_gpu(tmp_path):
-    mp.spawn(_worker, args=(_port(), str(tmp_path)), nprocs=WORLD, join=True)
+@pytest.mark.parametrize("world,batched", [(2, False), (2, True), (4, True)])
+def test_head_parallel_matches_one_gpu(tmp_path, world, batched):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.spawn(_worker, args=(world, _port(), str(tmp_path), batched), nprocs=world, join=True)
     ref = _build(H, _labels(), "cuda:0")
     want = []
     for blk, layers in enumerate(_inputs()):
@@ -92,7 +100,7 @@ def test_head_parallel_two_gpus_matches_one_gpu(tmp_path):
             for layer, (k, v, q) in enumerate(layers):
                 ref[layer].update(k.cuda(), v.cuda(), start, cache_update_mode=mode)
                 want.append(ref[layer].attend(q.cuda(), start).cpu())
-    parts = [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) for r in range(WORLD)]
+    parts = [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) for r in range(world)]
     for i, w in enumerate(want):
-        got = torch.cat([parts[r][i] for r in range(WORLD)], dim=1)
+        got = torch.cat([parts[r][i] for r in range(world)], dim=1)
         assert torch.equal(got.view(torch.int16), w.view(torch.int16)), i

@@ -32,10 +32,10 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _init(rank: int, port: int) -> None:
+def _init(rank: int, port: int, world: int = WORLD) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
 
 
 def _oracle(labels):
@@ -103,22 +103,28 @@ def _worker_exchange(rank: int, port: int) -> None:
         dist.destroy_process_group()
 
 
-def _worker_cache(rank: int, port: int, expected) -> None:
+def _worker_cache(rank: int, port: int, expected, world: int = WORLD,
+                  batched: bool = False) -> None:
     from pyramidkv import head_parallel as hp
-    _init(rank, port)
+    _init(rank, port, world)
     try:
-        h0, h1 = hp.head_range(rank, WORLD, H)
-        t0, t1 = hp.token_range(rank, WORLD, F * FSEQ)
+        h0, h1 = hp.head_range(rank, world, H)
+        t0, t1 = hp.token_range(rank, world, F * FSEQ)
         orc = _oracle(_labels()[:, h0:h1])
-        layers = [hp.HeadParallelMegaCache(_OracleLayer(orc, l)) for l in range(L)]
+        ex = hp.HeadParallelExchange()
+        layers = [hp.HeadParallelMegaCache(_OracleLayer(orc, l), exchange=ex) for l in range(L)]
         shard = lambda a: torch.from_numpy(np.ascontiguousarray(a[:, t0:t1]).view(np.int16))  # noqa
         i = 0
         for blk, inputs in enumerate(_inputs()):
             start = blk * F * FSEQ
             for mode in ("noisy", "clean"):
                 for layer, (k, v, q) in enumerate(inputs):
-                    layers[layer].update(shard(k), shard(v), start, cache_update_mode=mode)
-                    out = layers[layer].attend(shard(q), start).numpy()
+                    if batched:   # Q, K and V in one exchange
+                        out = layers[layer].step(shard(q), shard(k), shard(v), start,
+                                                 cache_update_mode=mode).numpy()
+                    else:
+                        layers[layer].update(shard(k), shard(v), start, cache_update_mode=mode)
+                        out = layers[layer].attend(shard(q), start).numpy()
                     want = expected[i][:, t0:t1]
                     assert out.shape == want.shape, (out.shape, want.shape)
                     assert np.array_equal(out, want), (rank, blk, mode, layer,
@@ -142,3 +148,11 @@ def test_exchange_round_trip_two_ranks():
 
 def test_head_parallel_cache_matches_single_rank():
     mp.spawn(_worker_cache, args=(_free_port(), _expected()), nprocs=WORLD, join=True)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_parallel_step_one_exchange(world):
+    """``step``: Q, K and V travel in one all-to-all (2 and 4 ranks; at 4 ranks
+    each rank owns one head); outputs equal the single-rank run bit for bit."""
+    mp.spawn(_worker_cache, args=(_free_port(), _expected(), world, True), nprocs=world,
+             join=True)
