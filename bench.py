@@ -60,11 +60,13 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--kernel-case", choices=["attn", "attn-plain", "pack", "update"],
+    ap.add_argument("--kernel-case", choices=["attn", "attn-plain", "attn-c4", "pack", "update"],
                     default=None,
                     help="run one kernel on a standalone steady-state-sized input "
                          "(small device footprint, for profiler captures) and exit")
     ap.add_argument("--kernel-iters", type=int, default=4)
+    ap.add_argument("--batch", type=int, default=1,
+                    help="videos per attention launch of --kernel-case attn-c4 (configs[3])")
     ap.add_argument("--head-parallel", type=int, default=0, metavar="n",
                     help="split each video's heads over groups of n ranks (n divides 12 and "
                          "the rank count); the line then measures world/n head-parallel videos")
@@ -215,6 +217,40 @@ def clocks_stop(h):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+# Algorithmic bytes of the update stage (the per-unit figures of the path's
+# measurement contract): every pass writes each head's 3 new frames to sink or
+# recent, K and V read and written (2 * F * D * 2 * 2 B) plus the generated
+# positions (F * 3 * 8 B); a clean pass adds the middle frames (periodic heads:
+# all 3; stride heads: t % 6 == 0) at the same cost, and per merge head reads
+# the 3 frames' K/V (F * D * 2 * 2 B), read-modify-writes the fp32
+# accumulators of the 390 patch groups (390 * D * 4 * 2 * 2 B per frame) and
+# writes each completed 4-frame block's anchors (390 * D * 2 * 2 B).
+FRAME_KV_RW = 2 * FSEQ * D_ * 2 * 2
+FRAME_POS_W = FSEQ * 3 * 8
+MERGE_GROUPS = (HG_ // 2) * (W_ // 2)
+
+
+def update_algorithmic_bytes(labels, frames: int) -> float:
+    """B_upd per layer-step, averaged over one video of the label matrix."""
+    import numpy as np
+    labels = np.asarray(labels)
+    n_stride = int((labels == 1).sum())
+    n_cyclic = int((labels == 2).sum())
+    n_merge = int((labels == -1).sum())
+    heads_layers = labels.size
+    total = 0
+    for blk in range(frames // FRAMES_PER_BLOCK):
+        ts = range(blk * FRAMES_PER_BLOCK, (blk + 1) * FRAMES_PER_BLOCK)
+        # sink / recent writes of all passes, all heads of all layers
+        total += len(PASSES) * heads_layers * FRAMES_PER_BLOCK * (FRAME_KV_RW + FRAME_POS_W)
+        middle = n_cyclic * FRAMES_PER_BLOCK + n_stride * sum(1 for t in ts if t % 6 == 0)
+        total += middle * (FRAME_KV_RW + FRAME_POS_W)
+        finals = sum(1 for t in ts if t % 4 == 3)
+        total += n_merge * (FRAMES_PER_BLOCK * (FSEQ * D_ * 2 * 2 + MERGE_GROUPS * D_ * 4 * 2 * 2)
+                            + finals * MERGE_GROUPS * D_ * 2 * 2)
+    return total / layer_steps(frames)
+
+
 def layer_steps(frames: int) -> int:
     return (frames // FRAMES_PER_BLOCK) * len(PASSES) * L_
 
@@ -663,6 +699,16 @@ def run_ours(args, rank: int, world: int, local: int):
                           "peak": float(peaks["hbm_gbs"]),
                           "frac": pack_bytes / (pack / 1e3) / 1e9 / float(peaks["hbm_gbs"]),
                           "bytes_per_launch": pack_bytes / n_total},
+        "update_roofline": {"bound": "hbm", "unit": "GB/s",
+                            "achieved": update_algorithmic_bytes(w.labels, args.frames) /
+                            (upd / n_total / 1e3) / 1e9,
+                            "peak": float(peaks["hbm_gbs"]),
+                            "frac": update_algorithmic_bytes(w.labels, args.frames) /
+                            (upd / n_total / 1e3) / 1e9 / float(peaks["hbm_gbs"]),
+                            "bytes_per_layer_step": update_algorithmic_bytes(w.labels,
+                                                                             args.frames),
+                            "kernels": "route_kernel + copy_kernel (+ merge_kernel on clean "
+                                       "passes with merge heads)"},
         "kv_tokens_per_layer_step": tokens / n_total,
         "e2e": e2e,
         "gpu_launches": launches_per_video * args.steps,
@@ -681,6 +727,61 @@ def run_ours(args, rank: int, world: int, local: int):
                 args, rank, world, local, n, args.hp_steps, 1, with_e2e=False)
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def run_attn_c4(args):
+    """the ragged-attention microbench.  Per video and layer, each
+    of the 12 heads attends 4680 queries (3 chunks of 1560) to a K/V length
+    drawn uniformly from 3..21 frames of 1560 tokens (seed 0, a fresh draw per
+    layer); a launch covers one layer of `--batch` videos (batch x 12
+    segments of 4680 query rows), K/V ~ N(0, 1) bf16 standing for RoPE'd
+    keys.  30 layers are timed back to back (CUDA events per launch, after
+    warm-up), through the SM-balanced path MegaCache.attend uses."""
+    import torch
+    from pyramidkv import _ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ops = _ops.ops()
+    B, rows = args.batch, FRAMES_PER_BLOCK * FSEQ
+    g = torch.Generator(device="cpu").manual_seed(args.seed)
+    frames = torch.randint(3, 22, (L_, B * H_), generator=g)      # per layer, per (video, head)
+    lens = frames * FSEQ
+    cus = []
+    for l in range(L_):
+        cu = torch.zeros(B * H_ + 1, dtype=torch.int32)
+        cu[1:] = torch.cumsum(lens[l], 0).int()
+        cus.append(cu.to(dev))
+    T = int(lens.sum(1).max())
+    q = torch.randn(B * rows, H_, D_, generator=g).to(dev, torch.bfloat16)
+    k = torch.randn(T, D_, generator=g).to(dev, torch.bfloat16)
+    v = torch.randn(T, D_, generator=g).to(dev, torch.bfloat16)
+    ws = torch.zeros(int(ops.pkv_attention_ws_bytes(B, H_, rows)), dtype=torch.uint8, device=dev)
+    # video b's queries are rows [b*rows, (b+1)*rows) of every head: one
+    # "chunk" per video with rows_per_chunk = 4680, segment (b, h) = its K/V
+    run = lambda l: ops.pkv_attention_ws(q, k, v, cus[l], B, rows, D_ ** -0.5, ws)  # noqa
+    for _ in range(3):
+        for l in range(L_):
+            run(l)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L_)]
+    for l in range(L_):
+        ev[l][0].record()
+        run(l)
+        ev[l][1].record()
+    torch.cuda.synchronize()
+    ms = [e[0].elapsed_time(e[1]) for e in ev]
+    flops = [4.0 * rows * D_ * float(lens[l].sum()) for l in range(L_)]
+    peaks, kind = measured_peaks()
+    rate = sum(flops) / (sum(ms) / 1e3) / 1e12
+    print(json.dumps({
+        "kernel_case": "attn-c4", "batch": B, "layers": L_,
+        "us_per_layer": sum(ms) * 1e3 / L_, "tflops": rate,
+        "frac_of_sustained": rate / float(peaks["bf16_tflops_sustained"]),
+        "frac_of_burst": rate / float(peaks["bf16_tflops"]), "peak_source": kind,
+        "kv_frames_mean": float(frames.float().mean()),
+        "flop_per_layer": sum(flops) / L_,
+        "workload": "configs[3]: Q 4680/head, 12 heads, Lk ~ U{3..21} frames x 1560, "
+                    "30 layers, bf16, N(0,1) K/V"}), flush=True)
 
 
 def run_kernel_case(args):
@@ -784,6 +885,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.kernel_case == "attn-c4":
+        run_attn_c4(args)
         return
     if args.kernel_case:
         run_kernel_case(args)

@@ -332,7 +332,7 @@ constexpr int kThreads2 = 320;
 constexpr int kStages2 = 2;
 constexpr int kMaxSegLens = 1024;    // segment lengths / ranks staged in shared memory
 constexpr int kMaxCtas = kAttnMaxCtas;  // persistent grid bound (>= SM count)
-constexpr int kMaxSplitUnits = 1024;     // phase-2 units staged in shared memory
+constexpr int kMaxSplitUnits = 2048;     // phase-2 units staged in shared memory
 constexpr int64_t kPartFloats = kAttnPartFloats;  // O columns x rows, m, l, per-warp unit ids
 static_assert(kAttnPartFloats == 130 * kBM + 32, "partial block layout");
 

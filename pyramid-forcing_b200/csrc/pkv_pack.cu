@@ -176,8 +176,8 @@ constexpr int kPack128MaxSeg = 2048;  // plans with more segments use pack_kerne
 // ---------------------------------------------------------------------------
 // pack_bulk_kernel (head_dim 128): tiles of 64 tokens staged through shared
 // memory by bulk async copies.  One thread per block keeps a 2-stage ring of
-// (K, V, positions) tiles in flight with cp.async.bulk global -> shared (no
-// multicast); V goes straight back out with a bulk shared -> global store; the
+// (K, V, positions) tiles in flight with cp.async.bulk global -> shared (a
+// plain per-block copy); V goes straight back out with a bulk shared -> global store; the
 // block's threads read K (and positions) from shared memory, rotate and store
 // K and copy the positions.  A block holds up to 2 x 33.5 KB in flight without
 // spending registers on it, which a gather-copy needs to approach HBM rate.
