@@ -414,10 +414,25 @@ def cpu_baseline_json(fps, detail, cores):
             "us_per_layer_step": detail["us_per_layer_step"]}
 
 
+def host_threads():
+    """All host cores for the CPU legs: torchrun sets OMP_NUM_THREADS=1 when it
+    starts more than one process, which would leave numpy's BLAS on one
+    thread; the limit is lifted for the BLAS pools here and for the C pack by
+    the oracle's own thread count.  Returns (threads asked, BLAS pools' threads)."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        threadpool_limits(limits=n)
+        used = sorted({int(p.get("num_threads", 0)) for p in threadpool_info()})
+    except ImportError:  # pragma: no cover
+        used = []
+    return n, used
+
+
 def run_reference(args, rank: int):
     if rank != 0:
         return
-    cores = os.cpu_count()
+    cores, blas_threads = host_threads()
     fps_all = []
     detail = None
     for i in range(args.warmup + args.steps):
@@ -433,9 +448,22 @@ def run_reference(args, rank: int):
             "cpu_baseline": cpu_baseline_json(fps, detail, cores),
             "e2e": {"value": fps, "unit": "latent frames/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
-            "note": ("the reference path's own CPU code cannot run this workload (its planner "
-                     "needs a CUDA driver and its kernels are CUDA); timed is the oracle port "
-                     "of that path (oracle/pkv_oracle.c + numpy fp32 attention)")}
+            "sampled": True, "layer_steps_timed_per_step": 1,
+            "threads": {"asked": cores, "blas_pools": blas_threads,
+                        "c_pack": cores},
+            "parts": {"update (routing, state machine, frame copies, merge)":
+                      "port: oracle/pkv_oracle.c + oracle/pkv_oracle.py restating "
+                      "_mega_cache.py:136-414 and its kernels",
+                      "plan + pack with RoPE": "port: oracle/pkv_oracle.c restating "
+                      "mega_plan.cc and pyramidkv_pack.cu",
+                      "attention": "numpy fp32 BLAS standing in for flash_attn_varlen_func"},
+            "note": ("each step times one layer-step of the cache path at the 36-frame cache "
+                     "size (update, plan + pack, attention of the 36 (chunk, head) segments, "
+                     "scaled from the segments that fit a 4 s budget) and scales it to the "
+                     "6000 layer-steps of a 120-frame video; the value is the host's, the same "
+                     "at every GPU count.  The reference's own code for this path is CUDA "
+                     "kernels plus a host planner that needs a CUDA device; its Python parts "
+                     "cannot travel to the GPU box, so timed is the oracle port of that path")}
     print(json.dumps(line), flush=True)
 
 
@@ -716,6 +744,7 @@ def run_ours(args, rank: int, world: int, local: int):
         "device_status": status,
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        host_threads()
         fps_cpu, detail = cpu_sample(args)
         line["cpu_baseline"] = cpu_baseline_json(fps_cpu, detail, os.cpu_count())
     if world > 1 and args.hp_steps > 0:
