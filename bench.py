@@ -718,7 +718,7 @@ def run_ours(args, rank: int, world: int, local: int):
                      "frac_of_burst": achieved / float(peaks["bf16_tflops"]),
                      "flops_per_launch": attn_flops / n_total,
                      # DRAM bytes per launch: one ncu capture of the kernel case
-                     # (profiles/attn_tc2_kernel_steady_state.md), scaled by work
+                     # of the kernel case (bench.py --kernel-case attn), scaled by work
                      "traffic": ATTN_DRAM_BYTES_PER_FLOP * attn_flops / n_total,
                      "traffic_source": "ncu dram__bytes_read+write of the kernel case "
                                        "(351.1 MB / 0.492 TFLOP), scaled to this launch"},

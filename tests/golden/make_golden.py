@@ -241,7 +241,7 @@ def gen_api(reference: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from pyramidkv import _mega_state_ref as ref
