@@ -65,11 +65,15 @@ def parse():
                     help="run one kernel on a standalone steady-state-sized input "
                          "(small device footprint, for profiler captures) and exit")
     ap.add_argument("--kernel-iters", type=int, default=4)
+    ap.add_argument("--kernel-heads", type=int, default=H_,
+                    help="heads of the attn kernel cases (6 / 3: a head-parallel rank's share)")
     ap.add_argument("--batch", type=int, default=1,
                     help="videos per attention launch of --kernel-case attn-c4 (configs[3])")
     ap.add_argument("--head-parallel", type=int, default=0, metavar="n",
                     help="split each video's heads over groups of n ranks (n divides 12 and "
                          "the rank count); the line then measures world/n head-parallel videos")
+    ap.add_argument("--no-dit", action="store_true",
+                    help="skip the random-init DiT leg (latent frames/s over DiT wall time)")
     ap.add_argument("--hp-steps", type=int, default=3,
                     help="videos timed by the head-parallel leg added to N > 1 lines")
     return ap.parse_args()
@@ -662,6 +666,67 @@ def run_head_parallel_line(args, rank: int, world: int, local: int):
     print(json.dumps(line), flush=True)
 
 
+def dit_measure(args, local: int, cache_us_per_layer_step: float):
+    """configs[1] as defined: latent frames/s = frames / DiT wall time.  The
+    random-init causal Wan2.1-T2V-1.3B DiT (pyramid-forcing_b200/causal_dit)
+    generates one video of `--frames` latent frames (4 denoising steps + the
+    clean pass per 3-frame block) from seeded N(0,1) noise [1, 16, F, 60, 104]
+    and a seeded N(0,1) text context [1, 512, 4096] (text encoder and VAE
+    excluded), its self-attention on this library's MegaCache, cross-attention
+    on its ragged attention kernel, GEMMs on cuBLAS.  One 6-frame video warms
+    up; one full video is timed with CUDA events."""
+    import torch
+    from causal_dit import CausalWanDiT, WanConfig, generate_video
+    from pyramidkv import _mega_cache, policy
+    dev = torch.device("cuda", local)
+    cfg = WanConfig()
+    model = CausalWanDiT(cfg, dev, seed=args.seed)
+    labels = policy.random_labels(L_, H_, seed=args.seed, merge_fraction=args.merge_fraction)
+    caches = _mega_cache.build_mega_caches(
+        L_, H_, D_, FSEQ, 3, 24, 4, policy.compositions_from_labels(labels, "baseline"),
+        max_attend_chunks=8, device=str(dev), sink_time_mapping_mode="window_clamp",
+        sink_time_clamp_min=18, sink_time_clamp_max=21, spatial_width=W_, spatial_height=HG_,
+        freqs=model.freqs)
+    ctx = caches[0].ctx
+    init_states = ctx.states_bytes.clone()
+    g = torch.Generator(device=dev).manual_seed(2000 + args.seed)
+    text = torch.randn(1, cfg.text_len, cfg.text_dim, generator=g, device=dev)
+    noise = torch.randn(1, cfg.in_dim, args.frames, 2 * HG_, 2 * W_, generator=g, device=dev,
+                        dtype=torch.bfloat16)
+
+    def reset():
+        ctx.mgr.reset()
+        ctx.states_bytes.copy_(init_states)
+        if ctx.committed_vc is not None:
+            ctx.committed_vc.zero_()
+    reset()
+    generate_video(model, caches, noise[:, :, :6], text, generator=g)
+    torch.cuda.synchronize()
+    reset()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    out = generate_video(model, caches, noise, text, generator=g)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    status = ctx.check_status()
+    n_ls = layer_steps(args.frames)
+    res = {"value": args.frames / (ms / 1e3), "unit": "latent frames/s",
+           "ms_per_video": ms, "us_per_layer_step": ms * 1e3 / n_ls,
+           "cache_path_us_per_layer_step": cache_us_per_layer_step,
+           "cache_path_share": cache_us_per_layer_step / (ms * 1e3 / n_ls),
+           "finite": bool(torch.isfinite(out.float()).all().item()),
+           "device_status": status,
+           "workload": ("configs[1]: random-init causal Wan2.1-T2V-1.3B DiT (30 layers, dim 1536, "
+                        "12x128 heads, FFN 8960, patch 1x2x2), %d latent frames of 16x60x104 in "
+                        "3-frame blocks, timesteps 1000/750/500/250 + clean pass, seeded N(0,1) "
+                        "noise and [1,512,4096] text context; T5 and VAE excluded" % args.frames),
+           "videos_timed": 1, "warmup": "one 6-frame video"}
+    del model, caches
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args, rank: int, world: int, local: int):
     import torch
     torch.cuda.set_device(local)
@@ -747,6 +812,10 @@ def run_ours(args, rank: int, world: int, local: int):
         host_threads()
         fps_cpu, detail = cpu_sample(args)
         line["cpu_baseline"] = cpu_baseline_json(fps_cpu, detail, os.cpu_count())
+    if world == 1 and not args.no_dit:
+        del w
+        torch.cuda.empty_cache()
+        line["dit"] = dit_measure(args, local, line["us_per_layer_step"])
     if world > 1 and args.hp_steps > 0:
         n = world if H_ % world == 0 else (4 if world % 4 == 0 else 0)
         if n:
@@ -824,9 +893,10 @@ def run_kernel_case(args):
     torch.cuda.set_device(dev)
     g = torch.Generator(device="cpu").manual_seed(args.seed)
     C = FRAMES_PER_BLOCK
-    frames = torch.randint(8, 15, (C * H_,), generator=g)
-    lens = frames * FSEQ + (torch.rand(C * H_, generator=g) < 0.3).long() * 390
-    cu = torch.zeros(C * H_ + 1, dtype=torch.int32)
+    Hk = args.kernel_heads if args.kernel_case in ("attn", "attn-plain") else H_
+    frames = torch.randint(8, 15, (C * Hk,), generator=g)
+    lens = frames * FSEQ + (torch.rand(C * Hk, generator=g) < 0.3).long() * 390
+    cu = torch.zeros(C * Hk + 1, dtype=torch.int32)
     cu[1:] = torch.cumsum(lens, 0).int()
     T = int(cu[-1])
     ops = _ops.ops()
@@ -834,12 +904,12 @@ def run_kernel_case(args):
     if args.kernel_case in ("attn", "attn-plain"):
         # attn: the SM-balanced path MegaCache.attend runs (workspace given);
         # attn-plain: one CTA per (segment, query-tile pair), no workspace
-        q = torch.randn(1, C * FSEQ, H_, D_, generator=g).to(dev, torch.bfloat16)
+        q = torch.randn(1, C * FSEQ, Hk, D_, generator=g).to(dev, torch.bfloat16)
         k = torch.randn(T, D_, generator=g).to(dev, torch.bfloat16)
         v = torch.randn(T, D_, generator=g).to(dev, torch.bfloat16)
         cud = cu.to(dev)
         if args.kernel_case == "attn":
-            ws = torch.zeros(int(ops.pkv_attention_ws_bytes(C, H_, FSEQ)), dtype=torch.uint8,
+            ws = torch.zeros(int(ops.pkv_attention_ws_bytes(C, Hk, FSEQ)), dtype=torch.uint8,
                              device=dev)
             run = lambda: ops.pkv_attention_ws(q[0], k, v, cud, C, FSEQ, D_ ** -0.5, ws)  # noqa
         else:

@@ -103,6 +103,13 @@ typedef struct pkv_cache {
     void *scratch;                  /* pkv_scratch_bytes() bytes, 256-aligned */
     int64_t scratch_bytes;
     int32_t *status;                /* sticky PKV_ST_* word (nullable)        */
+    /* Device int64 (nullable).  When set, pkv_cache_update, pkv_attend,
+     * pkv_attend_pack and pkv_attend_noalloc read the block's first latent
+     * frame from here when their kernels run, in place of their first_t
+     * argument, so one captured CUDA graph of a layer step replays for every
+     * block (write the frame into it before each replay).  No counterpart in
+     * the reference, whose planner takes the time on the host. */
+    const int64_t *first_t_dev;
 } pkv_cache_t;
 
 /* sizeof(PerHeadState), the 600-byte per-(layer, head) strategy record.

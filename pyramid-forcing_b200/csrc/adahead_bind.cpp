@@ -235,8 +235,21 @@ class PyramidKVCacheManager : public torch::CustomClassHolder {
       c.scratch_bytes = scratch_.numel();
     }
     c.status = status_.data_ptr<int32_t>();
+    c.first_t_dev = time_src_.defined() ? time_src_.data_ptr<int64_t>() : nullptr;
     return c;
   }
+
+  // Not in the reference: the fused update / attend ops read the block's
+  // first latent frame from `t` (a device int64 scalar) when their kernels
+  // run, instead of their first_t argument, so a captured layer step replays
+  // for any block.  clear_block_time() returns to the argument.
+  void set_block_time(Tensor t) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kLong && t.numel() == 1 &&
+                    t.device() == device(),
+                "set_block_time: expected a one-element int64 tensor on the manager's device");
+    time_src_ = t;
+  }
+  void clear_block_time() { time_src_ = Tensor(); }
 
   c10::Device device() const { return arena_.device(); }
   at::ScalarType kv_dtype() const { return sink_k_.scalar_type(); }
@@ -244,6 +257,7 @@ class PyramidKVCacheManager : public torch::CustomClassHolder {
  private:
   int64_t L_, H_, D_, F_, ms_, mm_, mr_, mac_;
   Tensor arena_, scratch_;
+  Tensor time_src_;  // device int64 block time read by the kernels (undefined: the argument)
   Tensor sink_k_, sink_v_, middle_k_, middle_v_, recent_k_, recent_v_;
   Tensor sink_pos_, middle_pos_, recent_pos_;
   Tensor head_t_, write_idx_, valid_count_, strategy_;
@@ -947,7 +961,9 @@ TORCH_LIBRARY(adahead, m) {
       .def("max_attend_chunks", &PyramidKVCacheManager::max_attend_chunks)
       .def("max_pack_tokens", &PyramidKVCacheManager::max_pack_tokens)
       .def("status_word", &PyramidKVCacheManager::status_word)
-      .def("scratch", &PyramidKVCacheManager::scratch);
+      .def("scratch", &PyramidKVCacheManager::scratch)
+      .def("set_block_time", &PyramidKVCacheManager::set_block_time)
+      .def("clear_block_time", &PyramidKVCacheManager::clear_block_time);
 
   m.def("scatter_copy(Tensor src_ptrs, Tensor lengths, Tensor offsets, Tensor(a!) dst, "
         "int col_dim) -> ()");

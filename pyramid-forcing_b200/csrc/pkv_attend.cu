@@ -42,7 +42,8 @@ extern "C" int pkv_attend_pack(const pkv_cache_t* c, const uint8_t* states_layer
   auto s = static_cast<cudaStream_t>(stream);
   const int rc = launch_plan(c, states_layer, layer, ts, num_chunks, sink_mode, cmin, cmax, lag,
                        /*check_capacity=*/1, /*add_layer_offset=*/1, c->cu_seqlens_k, sk, sg,
-                       sln, dst, traw, tremap, total, token_counter, s);
+                       sln, dst, traw, tremap, total, token_counter, s,
+                       c->first_t_dev);
   if (rc != PKV_OK) return rc;
   const bool rope = ft != nullptr || fy != nullptr || fx != nullptr;
   return launch_pack(c, sk, sg, sln, dst, int(N), rope ? tremap : nullptr, ft, ft_rows,
@@ -185,7 +186,8 @@ extern "C" int pkv_attend_noalloc(const pkv_cache_t* c, const uint8_t* states_la
   auto s = static_cast<cudaStream_t>(stream);
   int rc = launch_plan(c, states_layer, layer, ts, num_chunks, sink_mode, cmin, cmax, lag,
                        /*check_capacity=*/1, /*add_layer_offset=*/1, c->cu_seqlens_k, sk, sg,
-                       sln, dst, traw, tremap, total, token_counter, s);
+                       sln, dst, traw, tremap, total, token_counter, s,
+                       c->first_t_dev);
   if (rc != PKV_OK) return rc;
   const bool rope = ft != nullptr || fy != nullptr || fx != nullptr;
   rc = launch_pack(c, sk, sg, sln, dst, int(n), rope ? tremap : nullptr, ft, ft_rows, ft_cols,

@@ -279,10 +279,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16(bool b_mn_major) {
 // segment-major, longest segment first, so the units of one segment are
 // neighbours and read its K/V from HBM once.
 //
-// Without a partial-result workspace (AttnArgs::part == nullptr) the grid has
-// one CTA per unit.  With it the grid is one persistent CTA per SM:
-//   * phase 1: CTA b runs unit b whole (the longest units, side by side as in
-//     the one-CTA-per-unit grid);
+// Without a partial-result workspace (AttnArgs::part == nullptr), or with
+// fewer units than a quarter of the SMs, the grid has one CTA per unit.
+// Otherwise it is one persistent CTA per SM:
+//   * phase 1 (only when the units outnumber the SMs): CTA b runs unit b
+//     whole (the longest units, side by side as in the one-CTA-per-unit grid);
 //   * phase 2: the remaining units are laid end to end on a cost axis (K/V
 //     steps x a per-step weight: a pair step costs more than a lone-tile
 //     step) and cut into one contiguous range per CTA, sized so that every
@@ -545,10 +546,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
   S.NU = a.n_seg * S.U;
   S.G = gridDim.x;
   S.staged = a.n_seg <= kMaxSegLens;
-  const bool split = a.part != nullptr && S.staged && S.NU > S.G &&
-                     S.NU - S.G <= kMaxSplitUnits && S.G <= kMaxCtas;
-  S.n1 = split ? S.G : S.NU;
-  S.n2 = split ? S.NU - S.G : 0;
+  // with a workspace: a whole first wave when the units outnumber the SMs,
+  // else every unit cut between the SMs (phase 2 only)
+  const bool split = a.part != nullptr && S.staged && S.G <= kMaxCtas &&
+                     (S.NU > S.G ? S.NU - S.G : S.NU) <= kMaxSplitUnits;
+  S.n1 = split ? (S.NU > S.G ? S.G : 0) : S.NU;
+  S.n2 = split ? S.NU - S.n1 : 0;
 
   if (threadIdx.x == 0) {
     sm.seg1 = -1;
@@ -620,7 +623,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const int per1 = (S.G + 31) / 32;
     const int c0 = min(S.G, lane * per1), c1e = min(S.G, c0 + per1);
     int64_t c1 = 0;
-    for (int i = c0; i < c1e; ++i) {
+    for (int i = c0; i < c1e && i < S.n1; ++i) {
       S.unit(i, seg, u, ntile, nkv);
       c1 += nkv > 0 ? int64_t(nkv) * (ntile == 2 ? a.w_pair : a.w_single) + a.w_fixed : 0;
     }
@@ -630,8 +633,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const double T = double(c1_all + P2 + int64_t(S.n2) * a.w_fixed) / S.G;
     double bl = 0.0;  // this lane's budgets: T - phase-1 cost, at least 0
     for (int i = c0; i < c1e; ++i) {
-      S.unit(i, seg, u, ntile, nkv);
-      const int64_t c = nkv > 0 ? int64_t(nkv) * (ntile == 2 ? a.w_pair : a.w_single) + a.w_fixed : 0;
+      int64_t c = 0;
+      if (i < S.n1) {
+        S.unit(i, seg, u, ntile, nkv);
+        c = nkv > 0 ? int64_t(nkv) * (ntile == 2 ? a.w_pair : a.w_single) + a.w_fixed : 0;
+      }
       bl += fmax(0.0, T - double(c));
     }
     double binc = bl;  // inclusive scan of the lane budget sums
@@ -646,9 +652,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
     for (int i = c0; i < c1e; ++i) {
       if (bsum > 0.0) {
         sm.bnd[i] = int64_t(acc * scale);
-        S.unit(i, seg, u, ntile, nkv);
-        const int64_t c =
-            nkv > 0 ? int64_t(nkv) * (ntile == 2 ? a.w_pair : a.w_single) + a.w_fixed : 0;
+        int64_t c = 0;
+        if (i < S.n1) {
+          S.unit(i, seg, u, ntile, nkv);
+          c = nkv > 0 ? int64_t(nkv) * (ntile == 2 ? a.w_pair : a.w_single) + a.w_fixed : 0;
+        }
         acc += fmax(0.0, T - double(c));
       } else {
         sm.bnd[i] = int64_t(double(P2) * (double(i) / S.G));
@@ -1217,8 +1225,11 @@ int launch_attention(const uint16_t* q, int64_t q_rs, int64_t q_hs, const uint16
       // outnumber the SMs (the schedule's arrays fit shared memory)
       int grid = int(units);
       const int G = sm_count() < kMaxCtas ? sm_count() : kMaxCtas;
-      if (ws != nullptr && ws->part != nullptr && ws->cnt != nullptr && units > G &&
-          units <= ws->cnt_units && n_seg <= kMaxSegLens && units - G <= kMaxSplitUnits) {
+      // (units fewer than a quarter of the SMs stay one CTA per unit: too
+      // little work to cut)
+      if (ws != nullptr && ws->part != nullptr && ws->cnt != nullptr && units * 4 > G &&
+          units <= ws->cnt_units && n_seg <= kMaxSegLens &&
+          (units > G ? units - G : units) <= kMaxSplitUnits) {
         a.part = ws->part;
         a.cnt = ws->cnt;
         grid = G;

@@ -19,6 +19,7 @@ struct MergeLaunch {
   const int64_t* new_pos;
   int pos_width;
   int64_t first_t;
+  const int64_t* t_dev;  // device first_t (nullable): replaces first_t when set
   const int32_t *dkind, *dslot, *dfin, *dnew;
   float *acc_k, *acc_v;
   int64_t* acc_pos;
@@ -42,7 +43,8 @@ int launch_plan(const pkv_cache_t* c, const uint8_t* states_layer, int layer,
                 const int64_t* current_t, int num_chunks, int sink_mode, int cmin, int cmax,
                 int lag, int check_capacity, int add_layer_offset, int32_t* cu, int32_t* sk,
                 int32_t* sg, int32_t* sl, int32_t* dst, int64_t* traw, int64_t* tremap,
-                int64_t* total, int64_t* counter, cudaStream_t stream);
+                int64_t* total, int64_t* counter, cudaStream_t stream,
+                const int64_t* t_dev = nullptr);
 
 int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, const int32_t* sl,
                 const int32_t* dst, int n_seg, const int64_t* tremap, const float* ft,

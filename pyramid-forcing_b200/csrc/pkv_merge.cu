@@ -42,7 +42,7 @@ __device__ __forceinline__ void pos_of(const MergeLaunch& m, int f, int h, int t
     y = static_cast<int32_t>(p[1]);
     x = static_cast<int32_t>(p[2]);
   } else {
-    pt = m.first_t + f;
+    pt = (m.t_dev != nullptr ? __ldg(m.t_dev) : m.first_t) + f;
     y = t / m.pos_width;
     x = t % m.pos_width;
   }
@@ -333,6 +333,7 @@ extern "C" int pkv_merge_accum(const uint8_t* states, const uint16_t* new_k,
   m.new_pos = new_pos;
   m.pos_width = 1;
   m.first_t = 0;
+  m.t_dev = nullptr;
   m.dkind = desc_dst_kind;
   m.dslot = desc_merge_accum_slot;
   m.dfin = desc_merge_finalize_completed_idx;

@@ -45,6 +45,7 @@ struct PlanArgs {
   int add_layer_offset, check_capacity;
   int64_t capacity;
   int64_t t[PKV_MAX_CHUNKS];
+  const int64_t* t_dev;  // device time of chunk 0 (nullable): chunk c at *t_dev + c
   int32_t *cu, *sk, *sg, *sl, *dst;
   int64_t *traw, *tremap;
   int64_t *total_out, *counter;
@@ -66,10 +67,16 @@ __device__ __forceinline__ int64_t map_sink_time(int64_t t, int mode, int cmin, 
 
 // Calls emit(kind, slot_in_layer, len, t_raw, t_remap) for every segment of
 // (chunk c, head h) in the reference's order; returns the segment count.
+// Time of chunk c: from the launch parameters, or chunk 0's time read from
+// device memory when the caller keeps it there (graph replay across blocks).
+__device__ __forceinline__ int64_t chunk_time(const PlanArgs& a, int c) {
+  return a.t_dev != nullptr ? __ldg(a.t_dev) + c : a.t[c];
+}
+
 template <class Emit>
 __device__ int walk_segments(const PlanArgs& a, int c, int h, Emit&& emit) {
   const HeadState& s = a.states[h];
-  const int64_t ct = a.t[c];
+  const int64_t ct = chunk_time(a, c);
   const int64_t sync_t = map_sink_time(ct, a.sink_mode, a.cmin, a.cmax, a.lag);
   const int thr = s.sink_capacity;
   const int64_t* vch = a.vc + (int64_t(a.layer) * a.H + h) * 3;
@@ -226,7 +233,7 @@ __device__ __forceinline__ bool plan_candidate(const PlanArgs& a, const PlanSmem
                                                int h, int j, int& kind, int& slot, int& len,
                                                int64_t& traw, int64_t& tremap) {
   const HeadState& s = sm.st[h];
-  const int64_t ct = a.t[c];
+  const int64_t ct = chunk_time(a, c);
   const int64_t sync_t = map_sink_time(ct, a.sink_mode, a.cmin, a.cmax, a.lag);
   const int thr = s.sink_capacity;
   if (j < kCandSink) {
@@ -417,7 +424,8 @@ int launch_plan(const pkv_cache_t* c, const uint8_t* states_layer, int layer,
                 const int64_t* current_t, int num_chunks, int sink_mode, int cmin, int cmax,
                 int lag, int check_capacity, int add_layer_offset, int32_t* cu, int32_t* sk,
                 int32_t* sg, int32_t* sl, int32_t* dst, int64_t* traw, int64_t* tremap,
-                int64_t* total, int64_t* counter, cudaStream_t stream) {
+                int64_t* total, int64_t* counter, cudaStream_t stream,
+                const int64_t* t_dev) {
   if (!c || !states_layer || !current_t || !cu || !sk || !sg || !sl || !dst || !traw ||
       !tremap || !c->valid_count || !c->merge_token_count)
     return PKV_EINVAL;
@@ -446,6 +454,7 @@ int launch_plan(const pkv_cache_t* c, const uint8_t* states_layer, int layer,
   a.check_capacity = check_capacity;
   a.capacity = c->max_pack_tokens;
   for (int i = 0; i < num_chunks; ++i) a.t[i] = current_t[i];
+  a.t_dev = t_dev;
   a.cu = cu;
   a.sk = sk;
   a.sg = sg;
@@ -496,5 +505,5 @@ extern "C" int pkv_plan(const pkv_cache_t* c, const uint8_t* states_layer, int l
                      sink_clamp_min, sink_clamp_max, decoupled_sink_lag, check_capacity,
                      add_layer_offset, cu_seqlens_k, src_kind, src_slot_global, seg_lengths,
                      dst_token_offsets, anchor_t_raw, anchor_t_remap, total_tokens,
-                     token_counter, static_cast<cudaStream_t>(stream));
+                     token_counter, static_cast<cudaStream_t>(stream), nullptr);
 }

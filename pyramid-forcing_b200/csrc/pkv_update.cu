@@ -290,11 +290,13 @@ struct RouteArgs {
   int64_t first_t;
   int pass_kind;
   int32_t* status;
+  const int64_t* t_dev;  // device first_t (nullable): replaces first_t when set
 };
 
 __global__ void route_kernel(RouteArgs a) {
   const int h = blockIdx.x * blockDim.x + threadIdx.x;
   if (h >= a.H) return;
+  const int64_t first_t = a.t_dev != nullptr ? __ldg(a.t_dev) : a.first_t;
   const int64_t vi = (int64_t(a.layer) * a.H + h) * 3;
   const int64_t sc = a.committed_vc[vi + 0];
   const int64_t mc = a.committed_vc[vi + 1];
@@ -351,7 +353,7 @@ __global__ void route_kernel(RouteArgs a) {
   if (a.pass_kind == 1) {
     HeadState s = a.states[h];
     for (int f = 0; f < a.F; ++f) {
-      const FrameDesc d = advance_head(s, static_cast<int32_t>(a.first_t + f), a.status);
+      const FrameDesc d = advance_head(s, static_cast<int32_t>(first_t + f), a.status);
       write_desc(a.desc, h * a.F + f, d, f, h);
       if (d.kind == kDstMiddle) {
         if (d.slot >= 0 && d.slot < a.max_middle) push(f, kDstMiddle, 0, d.slot);
@@ -380,10 +382,12 @@ struct CopyArgs {
   int layer, H, FSEQ, D, W;
   int max_sink, max_middle, max_recent;
   int64_t first_t;
+  const int64_t* t_dev;  // device first_t (nullable): replaces first_t when set
 };
 
 template <bool kVec>
 __global__ void copy_kernel(CopyArgs a) {
+  const int64_t first_t = a.t_dev != nullptr ? __ldg(a.t_dev) : a.first_t;
   const int tiles = (a.FSEQ + kTileTokens - 1) / kTileTokens;
   const int slots[3] = {a.max_sink, a.max_middle, a.max_recent};
   for (int u = blockIdx.x; u < a.H * tiles; u += gridDim.x) {
@@ -418,7 +422,7 @@ __global__ void copy_kernel(CopyArgs a) {
           copy_rows<kVec>(a.committed_v + (crow + slot) * a.FSEQ * a.D, sv, a.tok_stride, tok0,
                           ntok, a.D);
         }
-        const int64_t t = a.first_t + src;
+        const int64_t t = first_t + src;
         for (int r = threadIdx.x; r < ntok; r += blockDim.x) {
           const int tok = tok0 + r;
           const int64_t y = tok / a.W, x = tok % a.W;
@@ -564,7 +568,7 @@ extern "C" int pkv_cache_update(const pkv_cache_t* c, uint8_t* states, int layer
   RouteArgs ra{c->valid_count, c->committed_vc, c->sink_caps,
                reinterpret_cast<HeadState*>(layer_states), desc, items, counts, items_per_head,
                layer, H, frames, c->max_sink, c->max_middle, c->max_recent, first_t, pass_kind,
-               c->status};
+               c->status, c->first_t_dev};
   route_kernel<<<(H + 127) / 128, 128, 0, s>>>(ra);
   int rc = launch_status();
   if (rc != PKV_OK) return rc;
@@ -590,6 +594,7 @@ extern "C" int pkv_cache_update(const pkv_cache_t* c, uint8_t* states, int layer
   ca.max_middle = c->max_middle;
   ca.max_recent = c->max_recent;
   ca.first_t = first_t;
+  ca.t_dev = c->first_t_dev;
   const int tiles = (c->frame_seqlen + kTileTokens - 1) / kTileTokens;
   const int grid = grid_for(int64_t(H) * tiles);
   const bool vec = (c->head_dim % 8 == 0) && (tok_stride % 8 == 0) && (head_stride % 8 == 0) &&
@@ -614,6 +619,7 @@ extern "C" int pkv_cache_update(const pkv_cache_t* c, uint8_t* states, int layer
     m.new_pos = nullptr;
     m.pos_width = ca.W;
     m.first_t = first_t;
+    m.t_dev = c->first_t_dev;
     m.dkind = desc.kind;
     m.dslot = desc.accum_slot;
     m.dfin = desc.finalize_idx;

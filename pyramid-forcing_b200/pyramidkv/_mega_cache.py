@@ -75,6 +75,18 @@ class MegaCacheCtx:
     # attend() (used to place CUDA events around the attention kernel)
     on_stage: object = None
 
+    def device_block_time(self) -> torch.Tensor:
+        """Make the kernels read the block's first latent frame from a device
+        int64 scalar (returned) instead of ``current_start``: write
+        ``current_start // frame_seqlen`` into it before each layer step, and
+        one captured CUDA graph of a layer step replays for every block.  Not
+        in the reference (whose planner takes the time on the host)."""
+        if getattr(self, "_block_time", None) is None:
+            self._block_time = torch.zeros(1, dtype=torch.int64,
+                                           device=self.states_bytes.device)
+            self.mgr.set_block_time(self._block_time)
+        return self._block_time
+
     def check_status(self) -> int:
         """Synchronise, read and clear the device status word; raise on errors."""
         st = int(_ops.ops().pkv_status(self.mgr))

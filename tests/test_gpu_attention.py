@@ -170,3 +170,22 @@ def test_balanced_attention_ragged_edges(cuda):
     for i in empty:
         c, h = divmod(i, H)
         assert out[c * Lq:(c + 1) * Lq, h].abs().max().item() == 0.0
+
+
+def test_balanced_attention_fewer_units_than_sms(cuda):
+    """Fewer units than SMs (a head-parallel rank's share: 3 chunks x 3 heads x
+    7 units = 63): every unit's keys are cut between the SMs and recombined."""
+    from pyramidkv import _ops
+    C, H, Lq, D = 3, 3, 1560, 128
+    g = torch.Generator().manual_seed(31)
+    frames = torch.randint(4, 20, (C * H,), generator=g)
+    lens = (frames * 1560 + (torch.rand(C * H, generator=g) < 0.3).long() * 390).tolist()
+    q, k, v, cu = _case(cuda, C, H, Lq, D, lens, seed=4)
+    ws = _ws(cuda, C, H, Lq)
+    scale = D ** -0.5
+    out = _ops.ops().pkv_attention_ws(q, k, v, cu, C, Lq, scale, ws)
+    torch.cuda.synchronize()
+    assert int(_ws_counters(ws).abs().sum()) == 0
+    _check(out, _reference(q, k, v, cu, C, H, Lq, scale))
+    again = _ops.ops().pkv_attention_ws(q, k, v, cu, C, Lq, scale, ws)
+    assert torch.equal(again.view(torch.int16), out.view(torch.int16))

@@ -50,7 +50,7 @@ class PkvCache(ctypes.Structure):
                                     "cu_seqlens_k", "committed_vc", "committed_recent_k",
                                     "committed_recent_v", "committed_recent_pos", "sink_caps",
                                     "scratch")]
-                + [("scratch_bytes", I64), ("status", P)])
+                + [("scratch_bytes", I64), ("status", P), ("first_t_dev", P)])
 
 
 def _describe(ctx) -> PkvCache:
