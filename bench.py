@@ -60,7 +60,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--kernel-case", choices=["attn", "attn-plain", "attn-c4", "pack", "update"],
+    ap.add_argument("--kernel-case",
+                    choices=["attn", "attn-plain", "attn-c4", "attn-d64", "pack", "update",
+                             "rope-q", "chunk-copy"],
                     default=None,
                     help="run one kernel on a standalone steady-state-sized input "
                          "(small device footprint, for profiler captures) and exit")
@@ -74,6 +76,9 @@ def parse():
                          "the rank count); the line then measures world/n head-parallel videos")
     ap.add_argument("--no-dit", action="store_true",
                     help="skip the random-init DiT leg (latent frames/s over DiT wall time)")
+    ap.add_argument("--hp-exchange", choices=["peer", "nccl"], default="peer",
+                    help="head-parallel exchange: NVLink peer stores into symmetric memory, "
+                         "or NCCL all_to_all_single")
     ap.add_argument("--hp-steps", type=int, default=3,
                     help="videos timed by the head-parallel leg added to N > 1 lines")
     return ap.parse_args()
@@ -489,7 +494,7 @@ class HPWorkload:
     Q/K/V sets (the same seeded video on every rank of the group)."""
 
     @staticmethod
-    def build(device, seed: int, group, merge_fraction=None):
+    def build(device, seed: int, group, merge_fraction=None, exchange="peer"):
         import torch
         import torch.distributed as dist
         from pyramidkv import head_parallel as hp, policy
@@ -501,7 +506,8 @@ class HPWorkload:
         labels = policy.random_labels(L_, H_, seed=seed, merge_fraction=merge_fraction)
         comps = policy.compositions_from_labels(labels, "baseline")
         w.caches = hp.build_head_parallel_caches(
-            L_, H_, D_, FSEQ, 3, 24, 4, comps, group=group, max_attend_chunks=8,
+            L_, H_, D_, FSEQ, 3, 24, 4, comps, group=group, exchange=exchange,
+            block_tokens=FRAMES_PER_BLOCK * FSEQ, max_attend_chunks=8,
             device=str(device), sink_time_mapping_mode="window_clamp", sink_time_clamp_min=18,
             sink_time_clamp_max=21, spatial_width=W_, spatial_height=HG_, freqs=rope_table(D_))
         w.ctx = w.caches[0].local.ctx
@@ -551,7 +557,7 @@ def head_parallel_measure(args, rank: int, world: int, local: int, n: int, steps
     gi = rank // n
     dev = torch.device("cuda", local)
     w = HPWorkload.build(dev, seed=args.seed + gi, group=groups[gi],
-                         merge_fraction=args.merge_fraction)
+                         merge_fraction=args.merge_fraction, exchange=args.hp_exchange)
     for _ in range(warmup):
         w.reset()
         run_video_hp(w, args.frames)
@@ -596,12 +602,16 @@ def head_parallel_measure(args, rank: int, world: int, local: int, n: int, steps
            "scaling": "strong within a group (one video's heads over n GPUs)",
            "us_per_layer_step": ms * 1e3 / tot,
            "breakdown_us_per_layer_step_rank": {
-               "exchange_in (pack Q/K/V + all_to_all)": ex_in,
+               "exchange_in (pack + transfer of Q/K/V)": ex_in,
                "cache (update + plan/pack + attention)": cache,
-               "exchange_out (all_to_all + scatter O)": ex_out},
+               "exchange_out (transfer + scatter of O)": ex_out},
            "heads_per_rank": H_ // n, "tokens_per_rank": lt,
            "nvlink_bytes_per_layer_step_rank": {"qkv": bytes_in, "out": bytes_out},
-           "collective": "torch.distributed all_to_all_single (NCCL), Q/K/V together, O back",
+           "collective": ("NVLink peer stores into symmetric-memory buffers (pack kernel writes "
+                          "each rank's Q/K/V share into its receive buffer; the output pass "
+                          "writes each token owner's rows at this rank's heads), one barrier per "
+                          "exchange" if args.hp_exchange == "peer" else
+                          "torch.distributed all_to_all_single (NCCL), Q/K/V together, O back"),
            "clocks": clocks}
     if with_e2e:
         from pyramidkv.host_staging import HostStaging
@@ -915,6 +925,40 @@ def run_kernel_case(args):
         else:
             run = lambda: ops.pkv_attention(q[0], k, v, cud, C, FSEQ, D_ ** -0.5)  # noqa: E731
         work, unit = 4.0 * FSEQ * D_ * T, "FLOP"
+    elif args.kernel_case == "attn-d64":
+        # the CUDA-core kernel (head_dim other than 128): 3 chunks x 4 heads of
+        # 1560 queries over 2-4 frames each, head_dim 64
+        Hs, Ds = 4, 64
+        lens_s = (torch.randint(2, 5, (C * Hs,), generator=g) * FSEQ)
+        cu_s = torch.zeros(C * Hs + 1, dtype=torch.int32)
+        cu_s[1:] = torch.cumsum(lens_s, 0).int()
+        Ts = int(cu_s[-1])
+        q = torch.randn(C * FSEQ, Hs, Ds, generator=g).to(dev, torch.bfloat16)
+        k = torch.randn(Ts, Ds, generator=g).to(dev, torch.bfloat16)
+        v = torch.randn(Ts, Ds, generator=g).to(dev, torch.bfloat16)
+        cud = cu_s.to(dev)
+        run = lambda: ops.pkv_attention(q, k, v, cud, C, FSEQ, Ds ** -0.5)  # noqa: E731
+        work, unit = 4.0 * FSEQ * Ds * Ts, "FLOP"
+    elif args.kernel_case == "rope-q":
+        # the model's query RoPE of one block: [4680, 12, 128] bf16 at frame 30
+        from pyramidkv.rope import causal_rope_apply
+        x = torch.randn(1, C * FSEQ, H_, D_, generator=g).to(dev, torch.bfloat16)
+        freqs = rope_table(D_).to(dev)
+        run = lambda: causal_rope_apply(x, None, freqs, start_frame=30,  # noqa: E731
+                                        grid_int=((C, HG_, W_),))
+        work, unit = 2 * x.numel() * 2, "B"
+    elif args.kernel_case == "chunk-copy":
+        # the head-parallel pack of one rank's token shard (x2): Q, K, V
+        # [2340, 12, 128] into the by-destination send layout, in this GPU's memory
+        n = 2
+        xs = [torch.randn(1, C * FSEQ // n, H_, D_, generator=g).to(dev, torch.bfloat16)
+              for _ in range(3)]
+        lt, hl = C * FSEQ // n, H_ // n
+        send = torch.empty(n, lt, 3, hl, D_, device=dev, dtype=torch.bfloat16)
+        run = lambda: ops.pkv_chunk_copy(xs, [x.stride(1) for x in xs],  # noqa: E731
+                                         [hl * x.stride(2) for x in xs], send, 3 * hl * D_,
+                                         lt * 3 * hl * D_, hl * D_, lt, n, hl * D_)
+        work, unit = 2 * 3 * xs[0].numel() * 2, "B"
     elif args.kernel_case == "update":
         # one layer with a third of its heads merge heads, after 30 blocks; a
         # run is the noisy and the clean update of the next block (route, copy

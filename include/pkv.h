@@ -361,6 +361,19 @@ int pkv_chunk_copy(const uint16_t *const *srcs, const int64_t *src_tok_strides,
                    int64_t dst_tok_stride, int64_t dst_group_stride, int64_t dst_src_stride,
                    int64_t tokens, int groups, int group_elems, pkv_stream_t stream);
 
+/*
+ * pkv_chunk_copy with one destination base per group (groups <= 8): chunk
+ * (source i, token t, group g) goes to dsts[g] + t*dst_tok_stride +
+ * i*dst_src_stride.  dsts may be other GPUs' buffers mapped into this process
+ * (symmetric memory): the head-parallel exchange writes each rank's share
+ * straight into that rank's receive buffer over NVLink, then the ranks
+ * barrier.  No counterpart in the reference.
+ */
+int pkv_chunk_copy_peers(const uint16_t *const *srcs, const int64_t *src_tok_strides,
+                         const int64_t *src_group_strides, int count, uint16_t *const *dsts,
+                         int64_t dst_tok_stride, int64_t dst_src_stride, int64_t tokens,
+                         int groups, int group_elems, pkv_stream_t stream);
+
 /* ---- AdaptiveKVCache / CppStrategyManager ops (not on the MegaCache path) ----
  * Same bytes as the reference's kernels; launched on `stream` (the
  * reference's use the legacy default stream).  One CTA per segment / frame.

@@ -708,6 +708,33 @@ void op_chunk_copy(std::vector<Tensor> srcs, std::vector<int64_t> src_ts,
            "pkv_chunk_copy");
 }
 
+// pkv_chunk_copy_peers: dst_ptrs are device addresses (this process's
+// mappings of each group's destination buffer, e.g. symmetric-memory peers).
+void op_chunk_copy_peers(std::vector<Tensor> srcs, std::vector<int64_t> src_ts,
+                         std::vector<int64_t> src_gs, std::vector<int64_t> dst_ptrs,
+                         int64_t dst_ts, int64_t dst_is, int64_t tokens, int64_t group_elems) {
+  TORCH_CHECK(!srcs.empty() && srcs.size() <= 4 && src_ts.size() == srcs.size() &&
+                  src_gs.size() == srcs.size(),
+              "pkv_chunk_copy_peers: 1-4 sources with one token and one group stride each");
+  TORCH_CHECK(!dst_ptrs.empty() && dst_ptrs.size() <= 8,
+              "pkv_chunk_copy_peers: 1-8 destination groups");
+  const uint16_t* ptrs[4] = {};
+  for (size_t i = 0; i < srcs.size(); ++i) {
+    TORCH_CHECK(srcs[i].is_cuda() && srcs[i].scalar_type() == at::kBFloat16 &&
+                    srcs[i].device() == srcs[0].device(),
+                "pkv_chunk_copy_peers: sources must be bf16 tensors on one device");
+    ptrs[i] = reinterpret_cast<const uint16_t*>(srcs[i].data_ptr());
+  }
+  uint16_t* dsts[8] = {};
+  for (size_t g = 0; g < dst_ptrs.size(); ++g)
+    dsts[g] = reinterpret_cast<uint16_t*>(static_cast<uintptr_t>(dst_ptrs[g]));
+  const c10::cuda::CUDAGuard guard(srcs[0].device());
+  check_rc(pkv_chunk_copy_peers(ptrs, src_ts.data(), src_gs.data(), int(srcs.size()), dsts,
+                                dst_ts, dst_is, tokens, int(dst_ptrs.size()), int(group_elems),
+                                stream_of(srcs[0])),
+           "pkv_chunk_copy_peers");
+}
+
 // 3D RoPE of a query block of one sample: x [tokens, H, D] bf16 (last dim
 // contiguous), tables float64 [rows, cols * 2] (re, im) for the t / y / x
 // parts; returns a new [tokens, H, D] tensor (causal_model.py:30-63).
@@ -1035,6 +1062,9 @@ TORCH_LIBRARY(adahead, m) {
   m.def("pkv_chunk_copy(Tensor[] srcs, int[] src_tok_strides, int[] src_group_strides, "
         "Tensor(a!) dst, int dst_tok_stride, int dst_group_stride, int dst_src_stride, "
         "int tokens, int groups, int group_elems) -> ()");
+  m.def("pkv_chunk_copy_peers(Tensor[] srcs, int[] src_tok_strides, int[] src_group_strides, "
+        "int[] dst_ptrs, int dst_tok_stride, int dst_src_stride, int tokens, "
+        "int group_elems) -> ()");
   m.def("pkv_status(__torch__.torch.classes.adahead.PyramidKVCacheManager mgr) -> int");
   m.def("pkv_rope_rounding(int mode) -> int");
   m.def("pkv_rope_q(Tensor x, Tensor ft, Tensor fy, Tensor fx, int start_frame, int frames, "
@@ -1058,6 +1088,7 @@ TORCH_LIBRARY_IMPL(adahead, CUDA, m) {
   m.impl("pkv_attention", op_attention);
   m.impl("pkv_attention_ws", op_attention_ws);
   m.impl("pkv_chunk_copy", op_chunk_copy);
+  m.impl("pkv_chunk_copy_peers", op_chunk_copy_peers);
 }
 
 TORCH_LIBRARY_IMPL(adahead, CompositeExplicitAutograd, m) {

@@ -147,6 +147,76 @@ class HeadParallelExchange:
         return out
 
 
+class PeerHeadExchange:
+    """The same exchanges over NVLink peer memory, without NCCL on the data
+    path: every rank's receive and output buffers are symmetric memory
+    (``torch.distributed._symmetric_memory``), so the one pass that packs Q,
+    K and V (``adahead.pkv_chunk_copy_peers``) stores each destination rank's
+    share straight into that rank's receive buffer, and the one pass over the
+    attention output stores each token owner's rows straight into its
+    ``[L/n, H, D]`` output, at the rank's own heads.  After each pass the ranks
+    barrier on the stream (bounded wait).  Receive buffers alternate between
+    two, so a rank writing step i+1's data cannot overwrite what a slower peer
+    still reads from step i (it passes step i+1's first barrier only after
+    every peer has finished step i), and outputs rotate over three, so an
+    output stays valid for the next two steps (time for an asynchronous copy
+    out).  CUDA, bf16, fixed shapes per object; results equal
+    :class:`HeadParallelExchange`'s bit for bit (both are plain copies).  No
+    counterpart in the reference."""
+
+    def __init__(self, group, shard_shape, device, timeout_ms: int = 10000):
+        import torch.distributed._symmetric_memory as symm
+        self.group = group
+        self.n = _world(group)
+        self.rank = dist.get_rank(group)
+        _, lt, h, d = shard_shape
+        if h % self.n:
+            raise ValueError(f"{h} heads do not split over {self.n} ranks")
+        self.lt, self.h, self.d, self.hl = lt, h, d, h // self.n
+        self.timeout_ms = timeout_ms
+        gname = group.group_name if group is not None else dist.group.WORLD.group_name
+        self._recv, self._out = [], []
+        for _ in range(2):
+            recv = symm.empty(self.n, lt, 3, self.hl, d, dtype=torch.bfloat16, device=device)
+            self._recv.append((recv, symm.rendezvous(recv, gname)))
+        for _ in range(3):
+            out = symm.empty(lt, h, d, dtype=torch.bfloat16, device=device)
+            self._out.append((out, symm.rendezvous(out, gname)))
+        self._ir = self._io = 0
+
+    def to_heads(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> tuple:
+        """Q, K, V ``[1, L/n, H, D]`` -> three ``[1, L, H/n, D]`` views."""
+        from . import _ops
+        recv, hr = self._recv[self._ir]
+        self._ir ^= 1
+        n, lt, hl, d = self.n, self.lt, self.hl, self.d
+        blk = lt * 3 * hl * d                      # one source rank's block in a receive buffer
+        dst = [int(p) + 2 * self.rank * blk for p in hr.buffer_ptrs]
+        xs = (q, k, v)
+        _ops.ops().pkv_chunk_copy_peers(list(xs), [x.stride(1) for x in xs],
+                                        [hl * x.stride(2) for x in xs], dst, 3 * hl * d, hl * d,
+                                        lt, hl * d)
+        hr.barrier(channel=0, timeout_ms=self.timeout_ms)
+        flat = recv.view(n * lt, 3, hl, d)
+        return tuple(flat[:, i].unsqueeze(0) for i in range(3))
+
+    def to_tokens(self, x: torch.Tensor) -> torch.Tensor:
+        """``[1, L, H/n, D]`` (this rank's heads) -> ``[1, L/n, H, D]`` view of
+        one of this rank's three output buffers (valid for the next two
+        exchanges)."""
+        from . import _ops
+        out, ho = self._out[self._io]
+        self._io = (self._io + 1) % 3
+        lt, hl, d = self.lt, self.hl, self.d
+        xs = x[0] if x.is_contiguous() else x[0].contiguous()
+        # token chunk g (its lt rows) goes to rank g's output at this rank's heads
+        dst = [int(p) + 2 * self.rank * hl * d for p in ho.buffer_ptrs]
+        _ops.ops().pkv_chunk_copy_peers([xs], [hl * d], [lt * hl * d], dst, self.h * d, 0, lt,
+                                        hl * d)
+        ho.barrier(channel=0, timeout_ms=self.timeout_ms)
+        return out.unsqueeze(0)
+
+
 def tokens_to_heads(x: torch.Tensor, group=None) -> torch.Tensor:
     """``[1, L/n, H, D]`` (this rank's tokens, all heads) -> ``[1, L, H/n, D]``
     (all tokens in order, this rank's heads); a fresh contiguous tensor."""
@@ -180,10 +250,16 @@ class HeadParallelMegaCache:
 
     def update(self, new_k: torch.Tensor, new_v: torch.Tensor, current_start: int,
                **kwargs) -> None:
+        if isinstance(self.exchange, PeerHeadExchange):
+            raise NotImplementedError("the peer-memory exchange moves Q, K and V together: "
+                                      "use step()")
         k, v = self.exchange.to_heads(new_k, new_v)
         self.local.update(k, v, current_start, **kwargs)
 
     def attend(self, q: torch.Tensor, current_start: int, **kwargs) -> torch.Tensor:
+        if isinstance(self.exchange, PeerHeadExchange):
+            raise NotImplementedError("the peer-memory exchange moves Q, K and V together: "
+                                      "use step()")
         (qh,) = self.exchange.to_heads(q)
         out = self.local.attend(qh, current_start, **kwargs)
         return self.exchange.to_tokens(out)
@@ -204,15 +280,26 @@ def build_head_parallel_caches(num_layers: int, num_heads: int, head_dim: int,
                                frame_seqlen: int, max_sink_frames: int,
                                max_middle_frames: int, max_recent_frames: int,
                                compositions: Sequence[Sequence], *, group=None,
+                               exchange: str = "nccl", block_tokens: int | None = None,
                                **kwargs) -> list[HeadParallelMegaCache]:
     """``build_mega_caches`` for this rank's heads of the full ``[L][H]``
     composition matrix, wrapped for the token-sharded model side; the layers
-    share one :class:`HeadParallelExchange`."""
+    share one exchange: ``"nccl"`` (:class:`HeadParallelExchange`) or
+    ``"peer"`` (:class:`PeerHeadExchange`, CUDA; needs ``block_tokens``, the
+    tokens of a block, to size its symmetric buffers; ``step`` only)."""
     from ._mega_cache import build_mega_caches
     rank, world = dist.get_rank(group), _world(group)
     h0, h1 = head_range(rank, world, num_heads)
     local = build_mega_caches(num_layers, h1 - h0, head_dim, frame_seqlen, max_sink_frames,
                               max_middle_frames, max_recent_frames,
                               [list(row)[h0:h1] for row in compositions], **kwargs)
-    ex = HeadParallelExchange(group)
+    if exchange == "peer":
+        if block_tokens is None or block_tokens % world:
+            raise ValueError("the peer exchange needs block_tokens divisible by the ranks")
+        ex = PeerHeadExchange(group, (1, block_tokens // world, num_heads, head_dim),
+                              kwargs.get("device", "cuda"))
+    elif exchange == "nccl":
+        ex = HeadParallelExchange(group)
+    else:
+        raise ValueError(f"unknown exchange {exchange!r}")
     return [HeadParallelMegaCache(c, group, ex) for c in local]

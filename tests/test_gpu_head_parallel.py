@@ -3,7 +3,9 @@
 Spawned ranks (one per GPU) each own 4/n of the 4 heads of a small model and
 feed ``HeadParallelMegaCache`` their token shard of every block, through the
 reference's two calls (``update`` then ``attend``: K and V in one exchange, Q
-in another) or through ``step`` (Q, K and V in one exchange).  The single-GPU
+in another) or through ``step`` (Q, K and V in one exchange), with the NCCL
+all-to-all exchange or the peer-memory one (symmetric memory: the pack kernel
+stores each rank's share into the other ranks' buffers over NVLink).  The single-GPU
 MegaCache over all heads runs on the same inputs; the gathered outputs of the
 ranks must equal it bit for bit (these shapes give every rank the same
 one-CTA-per-unit attention schedule as the single GPU).  Skipped with fewer
@@ -57,7 +59,8 @@ def _inputs():
     return [[(mk(), mk(), mk()) for _ in range(L)] for _ in range(BLOCKS)]
 
 
-def _worker(rank: int, world: int, port: int, out_dir: str, batched: bool) -> None:
+def _worker(rank: int, world: int, port: int, out_dir: str, batched: bool,
+            exchange: str = "nccl") -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = f"cuda:{rank}"
@@ -66,7 +69,9 @@ def _worker(rank: int, world: int, port: int, out_dir: str, batched: bool) -> No
                             device_id=torch.device("cuda", rank))
     try:
         from pyramidkv import head_parallel as hp
-        caches = _build(H, _labels(), dev, builder=hp.build_head_parallel_caches)
+        builder = lambda *a, **k: hp.build_head_parallel_caches(  # noqa: E731
+            *a, exchange=exchange, block_tokens=F * FSEQ, **k)
+        caches = _build(H, _labels(), dev, builder=builder)
         t0, t1 = hp.token_range(rank, world, F * FSEQ)
         got = []
         for blk, layers in enumerate(_inputs()):
@@ -87,11 +92,14 @@ def _worker(rank: int, world: int, port: int, out_dir: str, batched: bool) -> No
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,batched", [(2, False), (2, True), (4, True)])
-def test_head_parallel_matches_one_gpu(tmp_path, world, batched):
+@pytest.mark.parametrize("world,batched,exchange", [(2, False, "nccl"), (2, True, "nccl"),
+                                                    (4, True, "nccl"), (2, True, "peer"),
+                                                    (4, True, "peer")])
+def test_head_parallel_matches_one_gpu(tmp_path, world, batched, exchange):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.spawn(_worker, args=(world, _port(), str(tmp_path), batched), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _port(), str(tmp_path), batched, exchange), nprocs=world,
+             join=True)
     ref = _build(H, _labels(), "cuda:0")
     want = []
     for blk, layers in enumerate(_inputs()):
