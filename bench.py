@@ -1014,6 +1014,9 @@ def run_kernel_case(args):
     torch.cuda.synchronize()
     times = []
     for _ in range(args.kernel_iters):
+        # the GPU sleeps while the host enqueues the call, so the events time
+        # the device work and not the host's launch overhead
+        torch.cuda._sleep(1_000_000)
         ev[0].record()
         run()
         ev[1].record()

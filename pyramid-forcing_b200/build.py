@@ -28,7 +28,7 @@ NVCC = os.path.join(CUDA, "bin", "nvcc")
 
 CU_SOURCES = ["pkv_update.cu", "pkv_merge.cu", "pkv_plan.cu", "pkv_pack.cu", "pkv_attn.cu",
               "pkv_attend.cu", "pkv_legacy.cu", "pkv_rope.cu", "pkv_exchange.cu"]
-HEADERS = ["pkv_common.cuh", "pkv_internal.h"]
+HEADERS = ["pkv_common.cuh", "pkv_internal.h", "pkv_plan.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
            "--ptxas-options=-v"] + ARCH

@@ -6,12 +6,26 @@
 // pack, flash_attn_varlen_func).  The planner writes its descriptors into the
 // cache's scratch arena with the layer offset already applied, and
 // cu_seqlens_k into the cache's own cu_seqlens_k buffer.
+#include <cstdlib>
 #include <mutex>
 
 #include "pkv_common.cuh"
 #include "pkv_internal.h"
+#include "pkv_plan.cuh"
 
 using namespace pkv;
+
+namespace {
+// PKV_FUSED_PLAN_PACK=0 keeps the planner and the pack as two launches (the
+// same results; for comparing the two).
+bool fused_plan_pack() {
+  static const bool on = [] {
+    const char* e = std::getenv("PKV_FUSED_PLAN_PACK");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
+}  // namespace
 
 extern "C" int pkv_attend_pack(const pkv_cache_t* c, const uint8_t* states_layer, int layer,
                                int num_chunks, int64_t first_t, int sink_mode, int cmin,
@@ -40,12 +54,24 @@ extern "C" int pkv_attend_pack(const pkv_cache_t* c, const uint8_t* states_layer
   int64_t ts[PKV_MAX_CHUNKS];
   for (int i = 0; i < num_chunks; ++i) ts[i] = first_t + i;
   auto s = static_cast<cudaStream_t>(stream);
+  const bool rope = ft != nullptr || fy != nullptr || fx != nullptr;
+  if (!c->valid_count || !c->merge_token_count) return PKV_EINVAL;
+  if (layer < 0 || layer >= c->num_layers) return PKV_EINVAL;
+  {
+    // one launch: each pack block derives the segment list from the staged
+    // state records itself (the planner's rules), block 0 publishes cu_seqlens_k
+    const PlanArgs pa = plan_args(c, states_layer, layer, ts, num_chunks, sink_mode, cmin, cmax,
+                                  lag, /*check_capacity=*/1, /*add_layer_offset=*/1,
+                                  c->cu_seqlens_k, total, token_counter, c->first_t_dev);
+    if (fused_plan_pack() && plan_pack_fits(c, pa))
+      return launch_pack_planned(c, pa, ft, ft_rows, ft_cols, fy, fy_rows, fy_cols, fx, fx_rows,
+                                 fx_cols, s);
+  }
   const int rc = launch_plan(c, states_layer, layer, ts, num_chunks, sink_mode, cmin, cmax, lag,
                        /*check_capacity=*/1, /*add_layer_offset=*/1, c->cu_seqlens_k, sk, sg,
                        sln, dst, traw, tremap, total, token_counter, s,
                        c->first_t_dev);
   if (rc != PKV_OK) return rc;
-  const bool rope = ft != nullptr || fy != nullptr || fx != nullptr;
   return launch_pack(c, sk, sg, sln, dst, int(N), rope ? tremap : nullptr, ft, ft_rows,
                      ft_cols, fy, fy_rows, fy_cols, fx, fx_rows, fx_cols, s);
 }

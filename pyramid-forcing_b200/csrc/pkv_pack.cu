@@ -17,6 +17,8 @@
 // authority on which order nvcc's contraction picks, and the GPU parity tests
 // pin this choice against it.
 #include "pkv_common.cuh"
+#include "pkv_internal.h"
+#include "pkv_plan.cuh"
 
 namespace pkv {
 
@@ -208,6 +210,29 @@ struct BulkSmem {
   int warp_tot[kBulkThreads / 32];
 };
 
+// The pack that plans for itself (the path MegaCache.attend takes): the
+// layer's planner inputs, each (chunk, head)'s sync time and cyclic phase,
+// and per candidate segment of every (chunk, head) a descriptor and its
+// packed row.
+constexpr int kPlanPackMaxHeads = 16;
+constexpr int kPlanPackMaxPairs = kPack128MaxSeg / kCand;
+// descriptor: kind << 28 | remap source << 26 | slot in the layered pool
+constexpr uint32_t kRemapNone = 0, kRemapSync = 1, kRemapMedian = 2;
+constexpr int kDescSlotBits = 26;
+// The planner inputs (PlanStage) are only read before the first tile is
+// issued, so they borrow the stage buffers; the merge medians the producer
+// reads later are copied out of them.
+struct PlannedSmem {
+  uint32_t cand_desc[kPack128MaxSeg];
+  int cand_off[kPack128MaxSeg + 1];
+  int64_t pair_sync[kPlanPackMaxPairs];
+  int pair_phase[kPlanPackMaxPairs];
+  int64_t median[kPlanPackMaxHeads * kCandMerge];
+  int warp_tok[kBulkThreads / 32];
+};
+static_assert(sizeof(PlanStage<kPlanPackMaxHeads>) <= sizeof(BulkStage) * kBulkStages,
+              "the planner inputs fit the stage buffers");
+
 // Row r of a table with `rows` rows, clamped into [0, rows) (rows >= 1).
 __device__ __forceinline__ int clamp_row(int64_t r, int rows) {
   if (static_cast<uint64_t>(r) < static_cast<uint64_t>(rows)) return static_cast<int>(r);
@@ -259,55 +284,130 @@ __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
-__global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a) {
+// kPlanned: the segments are the planner's candidates (pkv_plan.cuh), which
+// every block evaluates itself from the staged state records; block 0 writes
+// cu_seqlens_k, the token total and the counter.  Otherwise they come from a
+// plan in global memory (sk / sg / sl / dst / tremap).
+template <bool kPlanned>
+__global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, PlanArgs pa) {
   extern __shared__ uint8_t pk_raw[];
   BulkSmem& sm = *reinterpret_cast<BulkSmem*>(
       (reinterpret_cast<uintptr_t>(pk_raw) + 127) & ~uintptr_t(127));
-  const int n = a.n_seg;
-  // ---- compact tile list (as pack128_kernel)
+  PlannedSmem& ps = *reinterpret_cast<PlannedSmem*>(
+      (reinterpret_cast<uintptr_t>(pk_raw) + 127 + sizeof(BulkSmem) + 127) & ~uintptr_t(127));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = kPlanned ? pa.C * pa.H * kCand : a.n_seg;
   const int per = (n + blockDim.x - 1) / blockDim.x;
   const int s_begin = min(n, int(threadIdx.x) * per), s_end = min(n, s_begin + per);
-  int run = 0;
-  for (int sg = s_begin; sg < s_end; ++sg) {
-    const int kind = a.sk[sg], len = a.sl[sg];
-    int nt = 0;
-    if (kind >= 0 && len > 0) {
-      if (kind > 3) {
-        if (blockIdx.x == 0) flag(a.status, PKV_ST_BAD_KIND);
-      } else {
-        nt = (len + kBulkTok - 1) / kBulkTok;
-      }
+  int run = 0, tok = 0;  // this thread's tiles and (planned) tokens
+  if (kPlanned) {
+    // ---- plan: every candidate's descriptor and length, in place of the
+    // planner's descriptor arrays
+    PlanStage<kPlanPackMaxHeads>& in = *reinterpret_cast<PlanStage<kPlanPackMaxHeads>*>(sm.st);
+    stage_plan_inputs(in, pa, threadIdx.x, blockDim.x);
+    __syncthreads();
+    for (int pr = threadIdx.x; pr < pa.C * pa.H; pr += blockDim.x) {
+      const int c = pr / pa.H, h = pr - c * pa.H;
+      const int64_t ct = chunk_time(pa, c);
+      ps.pair_sync[pr] = map_sink_time(ct, pa.sink_mode, pa.cmin, pa.cmax, pa.lag);
+      ps.pair_phase[pr] = head_phase(in.st[h], ct);
     }
-    sm.tile_start[sg] = nt;
-    run += nt;
+    for (int i = threadIdx.x; i < pa.H * kCandMerge; i += blockDim.x)
+      ps.median[i] = in.st[i / kCandMerge].done_median_t[i % kCandMerge];
+    __syncthreads();
+    for (int j = s_begin; j < s_end; ++j) {
+      const int pr = j / kCand, cand = j - pr * kCand;
+      const int h = pr % pa.H;
+      int kind = 0, slot = 0, len = 0;
+      int64_t traw = 0, tremap = -1;
+      if (!plan_candidate_at(pa, in, h, cand, ps.pair_sync[pr], ps.pair_phase[pr], kind, slot,
+                             len, traw, tremap))
+        len = 0;
+      const uint32_t src = tremap < 0 ? kRemapNone : kind == kSrcMerge ? kRemapMedian : kRemapSync;
+      ps.cand_desc[j] = uint32_t(kind) << 28 | src << kDescSlotBits |
+                        uint32_t(len > 0 ? layer_slot(pa, kind, slot) : 0);
+      ps.cand_off[j] = len;  // the length until the scan below
+      const int nt = (len + kBulkTok - 1) / kBulkTok;
+      sm.tile_start[j] = nt;
+      run += nt;
+      tok += len;
+    }
+    // the stage buffers' generic-proxy accesses end before the bulk copies
+    // (async proxy) write them
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  } else {
+    // ---- compact tile list (as pack128_kernel)
+    for (int sg = s_begin; sg < s_end; ++sg) {
+      const int kind = a.sk[sg], len = a.sl[sg];
+      int nt = 0;
+      if (kind >= 0 && len > 0) {
+        if (kind > 3) {
+          if (blockIdx.x == 0) flag(a.status, PKV_ST_BAD_KIND);
+        } else {
+          nt = (len + kBulkTok - 1) / kBulkTok;
+        }
+      }
+      sm.tile_start[sg] = nt;
+      run += nt;
+    }
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int incl = run;
+  int incl = run, tincl = tok;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
+    const int z = __shfl_up_sync(0xffffffffu, tincl, o);
+    if (lane >= o) {
+      incl += y;
+      tincl += z;
+    }
   }
-  if (lane == 31) sm.warp_tot[warp] = incl;
+  if (lane == 31) {
+    sm.warp_tot[warp] = incl;
+    if (kPlanned) ps.warp_tok[warp] = tincl;
+  }
   if (threadIdx.x == 0) {
     for (int st = 0; st < kBulkStages; ++st)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(pk_smem(&sm.full[st])));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  int before = 0, total = 0;
+  int before = 0, total = 0, tbefore = 0, ttotal = 0;
   for (int w = 0; w < int(blockDim.x >> 5); ++w) {
     if (w < warp) before += sm.warp_tot[w];
     total += sm.warp_tot[w];
+    if (kPlanned) {
+      if (w < warp) tbefore += ps.warp_tok[w];
+      ttotal += ps.warp_tok[w];
+    }
   }
-  int acc = before + incl - run;
+  int acc = before + incl - run, tacc = tbefore + tincl - tok;
   for (int sg = s_begin; sg < s_end; ++sg) {
     const int nt = sm.tile_start[sg];
     sm.tile_start[sg] = acc;
     acc += nt;
+    if (kPlanned) {
+      const int len = ps.cand_off[sg];
+      ps.cand_off[sg] = tacc;
+      tacc += len;
+    }
   }
-  if (threadIdx.x == 0) sm.tile_start[n] = total;
+  if (threadIdx.x == 0) {
+    sm.tile_start[n] = total;
+    if (kPlanned) ps.cand_off[n] = ttotal;
+  }
   __syncthreads();
+  if (kPlanned && blockIdx.x == 0) {
+    // the planner's outputs: cu_seqlens_k, the token total and counter
+    const int npair = pa.C * pa.H;
+    for (int pr = threadIdx.x; pr <= npair; pr += blockDim.x) pa.cu[pr] = ps.cand_off[pr * kCand];
+    if (threadIdx.x == 0) {
+      if (pa.total_out) *pa.total_out = ttotal;
+      if (pa.counter)
+        atomicAdd(reinterpret_cast<unsigned long long*>(pa.counter),
+                  static_cast<unsigned long long>(ttotal));
+      if (pa.check_capacity && int64_t(ttotal) > pa.capacity) flag(pa.status, PKV_ST_PACK_OVERFLOW);
+    }
+  }
 
   const int per_block = (total + int(gridDim.x) - 1) / int(gridDim.x);
   const int u_begin = min(total, int(blockIdx.x) * per_block);
@@ -329,8 +429,28 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a) {
     while (sm.tile_start[iseg + 1] <= u) ++iseg;
     const int st = i % kBulkStages;
     BulkTileMeta& m = sm.meta[st];
-    const int kind = a.sk[iseg], len = a.sl[iseg];
-    const int64_t slot = a.sg[iseg], dst0 = a.dst[iseg];
+    int kind, len;
+    int64_t slot, dst0, seg_tremap;
+    if (kPlanned) {
+      const uint32_t d = ps.cand_desc[iseg];
+      kind = int(d >> 28);
+      slot = int64_t(d & ((1u << kDescSlotBits) - 1u));
+      dst0 = ps.cand_off[iseg];
+      len = ps.cand_off[iseg + 1] - ps.cand_off[iseg];
+      const uint32_t src = (d >> kDescSlotBits) & 3u;
+      const int pr = iseg / kCand;
+      seg_tremap = src == kRemapSync ? ps.pair_sync[pr]
+                   : src == kRemapMedian
+                       ? ps.median[(pr % pa.H) * kCandMerge + iseg - pr * kCand -
+                                   (kCandSink + kCandRecent + kCandMiddle)]
+                       : int64_t(-1);
+    } else {
+      kind = a.sk[iseg];
+      len = a.sl[iseg];
+      slot = a.sg[iseg];
+      dst0 = a.dst[iseg];
+      seg_tremap = a.tremap != nullptr ? a.tremap[iseg] : -1;
+    }
     const int stride_tok = kind == kSrcMerge ? a.MTPA : a.F;
     const int tok0 = (u - sm.tile_start[iseg]) * kBulkTok;
     m.kind = kind;
@@ -347,7 +467,7 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a) {
       return;
     }
     m.src_row = slot * stride_tok + tok0;
-    m.tm = (a.rope && a.pos[kind] != nullptr) ? a.tremap[iseg] : -1;
+    m.tm = (a.rope && a.pos[kind] != nullptr) ? seg_tremap : -1;
     // 16-byte rule of the bulk copy: 24 * src_row and 24 * ntok must be multiples of 16
     m.pos_in_smem = a.pos[kind] != nullptr && (m.src_row & 1) == 0 && (m.ntok & 1) == 0;
     const uint32_t kv_bytes = uint32_t(m.ntok) * 256;
@@ -455,13 +575,12 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a) {
   }
 }
 
-int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, const int32_t* sl,
-                const int32_t* dst, int n_seg, const int64_t* tremap, const float* ft,
-                int ft_rows, int ft_cols, const float* fy, int fy_rows, int fy_cols,
-                const float* fx, int fx_rows, int fx_cols, cudaStream_t stream) {
-  if (n_seg == 0) return PKV_OK;
-  if (!c || !sk || !sg || !sl || !dst || n_seg < 0 || !c->k_flat || !c->v_flat)
-    return PKV_EINVAL;
+namespace {
+
+// The pools, the packed outputs and the RoPE tables of a pack launch.
+PackArgs pack_args(const pkv_cache_t* c, const float* ft, int ft_rows, int ft_cols,
+                   const float* fy, int fy_rows, int fy_cols, const float* fx, int fx_rows,
+                   int fx_cols) {
   PackArgs a{};
   const int64_t lh = int64_t(c->num_layers) * c->num_heads;
   a.k[0] = c->sink_k; a.v[0] = c->sink_v; a.pos[0] = c->sink_pos; a.rows[0] = lh * c->max_sink;
@@ -476,9 +595,6 @@ int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, cons
   a.v_out = c->v_flat;
   a.pos_out = c->pos_flat;
   a.out_rows = c->max_pack_tokens;
-  a.sk = sk; a.sg = sg; a.sl = sl; a.dst = dst;
-  a.n_seg = n_seg;
-  a.tremap = tremap;
   a.ft = ft; a.fy = fy; a.fx = fx;
   a.ft_rows = ft ? ft_rows : 0; a.ft_cols = ft ? ft_cols : 0;
   a.fy_rows = fy ? fy_rows : 0; a.fy_cols = fy ? fy_cols : 0;
@@ -486,46 +602,104 @@ int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, cons
   a.F = c->frame_seqlen;
   a.MTPA = c->max_merge_tokens;
   a.D = c->head_dim;
-  a.rope = tremap != nullptr && (ft != nullptr || fy != nullptr || fx != nullptr);
   a.rope_mode = g_rope_mode;
   a.status = c->status;
+  return a;
+}
+
+bool pack_vec_ok(const PackArgs& a) {
+  bool vec = (a.D % 8 == 0);
+  for (int i = 0; i < 4; ++i)
+    vec = vec && ((reinterpret_cast<uintptr_t>(a.k[i]) | reinterpret_cast<uintptr_t>(a.v[i])) % 16 == 0);
+  return vec;
+}
+
+// The bulk kernel's 16-byte rules: head_dim 128, every pool and output
+// 16-byte aligned, the segment list within the kernel's tile table.
+bool pack_bulk_ok(const PackArgs& a, int n_seg) {
+  return pack_vec_ok(a) && a.D == 128 && n_seg <= kPack128MaxSeg &&
+         ((reinterpret_cast<uintptr_t>(a.k_out) | reinterpret_cast<uintptr_t>(a.v_out)) % 16 == 0) &&
+         ((reinterpret_cast<uintptr_t>(a.pos[0]) | reinterpret_cast<uintptr_t>(a.pos[1]) |
+           reinterpret_cast<uintptr_t>(a.pos[2]) | reinterpret_cast<uintptr_t>(a.pos[3])) % 16 == 0);
+}
+
+template <bool kPlanned>
+constexpr int bulk_smem_bytes() {
+  return int(sizeof(BulkSmem)) + 128 + (kPlanned ? int(sizeof(PlannedSmem)) + 128 : 0);
+}
+
+// A persistent grid of exactly the resident blocks.
+template <bool kPlanned>
+int launch_bulk(const PackArgs& a, const PlanArgs& pa, cudaStream_t stream) {
+  static std::mutex mu;
+  static int per_sm_cache[kMaxDevices] = {};
+  constexpr int smem = bulk_smem_bytes<kPlanned>();
+  const int per_sm = per_device_once(per_sm_cache, mu, [] {
+    int n = 0;
+    if (cudaFuncSetAttribute(pack_bulk_kernel<kPlanned>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pack_bulk_kernel<kPlanned>,
+                                                      kBulkThreads, smem) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    return n < 1 ? 1 : n;
+  });
+  if (per_sm <= 0) return PKV_ELAUNCH;
+  pack_bulk_kernel<kPlanned><<<sm_count() * per_sm, kBulkThreads, smem, stream>>>(a, pa);
+  return launch_status();
+}
+
+}  // namespace
+
+int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, const int32_t* sl,
+                const int32_t* dst, int n_seg, const int64_t* tremap, const float* ft,
+                int ft_rows, int ft_cols, const float* fy, int fy_rows, int fy_cols,
+                const float* fx, int fx_rows, int fx_cols, cudaStream_t stream) {
+  if (n_seg == 0) return PKV_OK;
+  if (!c || !sk || !sg || !sl || !dst || n_seg < 0 || !c->k_flat || !c->v_flat)
+    return PKV_EINVAL;
+  PackArgs a = pack_args(c, ft, ft_rows, ft_cols, fy, fy_rows, fy_cols, fx, fx_rows, fx_cols);
+  a.sk = sk; a.sg = sg; a.sl = sl; a.dst = dst;
+  a.n_seg = n_seg;
+  a.tremap = tremap;
+  a.rope = tremap != nullptr && (ft != nullptr || fy != nullptr || fx != nullptr);
+  if (pack_bulk_ok(a, n_seg)) return launch_bulk<false>(a, PlanArgs{}, stream);
   const int max_len = a.F > a.MTPA ? a.F : a.MTPA;
   const int64_t units = int64_t(n_seg) * ((max_len + kPackTile - 1) / kPackTile);
   int64_t grid = int64_t(sm_count()) * 8;
   if (units < grid) grid = units;
   if (grid < 1) grid = 1;
-  bool vec = (a.D % 8 == 0);
-  for (int i = 0; i < 4; ++i)
-    vec = vec && ((reinterpret_cast<uintptr_t>(a.k[i]) | reinterpret_cast<uintptr_t>(a.v[i])) % 16 == 0);
-  const bool bulk_ok =
-      vec && a.D == 128 && n_seg <= kPack128MaxSeg &&
-      ((reinterpret_cast<uintptr_t>(a.k_out) | reinterpret_cast<uintptr_t>(a.v_out)) % 16 == 0) &&
-      ((reinterpret_cast<uintptr_t>(a.pos[0]) | reinterpret_cast<uintptr_t>(a.pos[1]) |
-        reinterpret_cast<uintptr_t>(a.pos[2]) | reinterpret_cast<uintptr_t>(a.pos[3])) % 16 == 0);
-  if (bulk_ok) {
-    // a persistent grid of exactly the resident blocks
-    static std::mutex mu;
-    static int per_sm_cache[kMaxDevices] = {};
-    const int smem = int(sizeof(BulkSmem)) + 128;
-    const int per_sm = per_device_once(per_sm_cache, mu, [smem] {
-      int n = 0;
-      if (cudaFuncSetAttribute(pack_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem) != cudaSuccess ||
-          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pack_bulk_kernel, kBulkThreads,
-                                                        smem) != cudaSuccess) {
-        cudaGetLastError();
-        return 0;
-      }
-      return n < 1 ? 1 : n;
-    });
-    if (per_sm <= 0) return PKV_ELAUNCH;
-    pack_bulk_kernel<<<sm_count() * per_sm, kBulkThreads, smem, stream>>>(a);
-  } else if (vec) {
+  if (pack_vec_ok(a)) {
     pack_kernel<true><<<int(grid), 256, 0, stream>>>(a);
   } else {
     pack_kernel<false><<<int(grid), 256, 0, stream>>>(a);
   }
   return launch_status();
+}
+
+bool plan_pack_fits(const pkv_cache_t* c, const PlanArgs& pa) {
+  // every valid candidate is a segment the planner would emit: at most
+  // max_sink + max_recent + 24 + 6 <= S of them per (chunk, head), so the
+  // planner's per-head cap never binds
+  if (!c || !c->k_flat || !c->v_flat || !pa.cu) return false;
+  if (!(pa.H <= kPlanPackMaxHeads && pa.C * pa.H * kCand <= kPack128MaxSeg &&
+        pa.max_sink <= kCandSink && pa.max_recent <= kCandRecent && pa.mmb <= kCandMerge &&
+        pa.max_middle + pa.mmb >= kCandMiddle + kCandMerge && pa.add_layer_offset == 1))
+    return false;
+  const PackArgs a = pack_args(c, nullptr, 0, 0, nullptr, 0, 0, nullptr, 0, 0);
+  for (int k = 0; k < 4; ++k)  // a slot fits its descriptor field
+    if (a.rows[k] > (int64_t(1) << kDescSlotBits)) return false;
+  return pack_bulk_ok(a, pa.C * pa.H * kCand);
+}
+
+int launch_pack_planned(const pkv_cache_t* c, const PlanArgs& pa, const float* ft, int ft_rows,
+                        int ft_cols, const float* fy, int fy_rows, int fy_cols, const float* fx,
+                        int fx_rows, int fx_cols, cudaStream_t stream) {
+  if (!plan_pack_fits(c, pa)) return PKV_EINVAL;
+  PackArgs a = pack_args(c, ft, ft_rows, ft_cols, fy, fy_rows, fy_cols, fx, fx_rows, fx_cols);
+  a.rope = ft != nullptr || fy != nullptr || fx != nullptr;
+  return launch_bulk<true>(a, pa, stream);
 }
 
 }  // namespace pkv

@@ -33,46 +33,12 @@
 // capacity check becomes a status bit the pack kernel also honours, so an
 // overflowing plan never writes out of bounds.
 #include "pkv_common.cuh"
+#include "pkv_plan.cuh"
 
 namespace pkv {
 
-struct PlanArgs {
-  const int64_t* vc;        // [L,H,3]
-  const int32_t* mtc;       // [L,H,MMB]
-  const HeadState* states;  // this layer's H records
-  int layer, H, F, max_sink, max_middle, max_recent, mmb, S, C;
-  int sink_mode, cmin, cmax, lag;
-  int add_layer_offset, check_capacity;
-  int64_t capacity;
-  int64_t t[PKV_MAX_CHUNKS];
-  const int64_t* t_dev;  // device time of chunk 0 (nullable): chunk c at *t_dev + c
-  int32_t *cu, *sk, *sg, *sl, *dst;
-  int64_t *traw, *tremap;
-  int64_t *total_out, *counter;
-  int32_t* status;
-};
-
-__device__ __forceinline__ int64_t map_sink_time(int64_t t, int mode, int cmin, int cmax,
-                                                 int lag) {
-  if (mode == 1) {
-    int64_t delta = t;
-    if (delta < cmin) delta = cmin;
-    if (delta > cmax) delta = cmax;
-    const int64_t out = t - delta;
-    return out < 0 ? 0 : out;
-  }
-  const int64_t out = t - lag;
-  return out < 0 ? 0 : out;
-}
-
 // Calls emit(kind, slot_in_layer, len, t_raw, t_remap) for every segment of
 // (chunk c, head h) in the reference's order; returns the segment count.
-// Time of chunk c: from the launch parameters, or chunk 0's time read from
-// device memory when the caller keeps it there (graph replay across blocks).
-__device__ __forceinline__ int64_t chunk_time(const PlanArgs& a, int c) {
-  return a.t_dev != nullptr ? __ldg(a.t_dev) + c : a.t[c];
-}
-
 template <class Emit>
 __device__ int walk_segments(const PlanArgs& a, int c, int h, Emit&& emit) {
   const HeadState& s = a.states[h];
@@ -204,101 +170,12 @@ __global__ void plan_kernel(PlanArgs a) {
   }
 }
 
-// ---------------------------------------------------------------------------
-// Warp-per-(chunk, head) planner.  Candidate j of a head (j < kCand) is:
-//   [0, 3)        sink slot j               valid while j < min(valid sink, cap)
-//   [3, 7)        recent slot j - 3         valid while < valid recent
-//   [7, 31)       middle slot j - 7         cyclic: inside the phase's buckets,
-//                                           stride / lag: inside the tkey ring
-//   [31, 37)      merge completed entry j - 31
-// (the pools' compiled bounds: 3 sink, 4 recent, 24 middle, 6 merge slots).
-// A lane's candidate is emitted at position (valid candidates before it)
-// unless that position reaches S, which is where the reference walk stops.
-// ---------------------------------------------------------------------------
 constexpr int kPlanWarpThreads = 1024;
-constexpr int kCandSink = 3, kCandRecent = 4, kCandMiddle = 24, kCandMerge = 6;
-constexpr int kCand = kCandSink + kCandRecent + kCandMiddle + kCandMerge;  // 37
-constexpr int kPlanMaxHeads = 64;
 
 struct PlanSmem {
-  HeadState st[kPlanMaxHeads];
-  int64_t vc[kPlanMaxHeads * 3];
-  int32_t mtc[kPlanMaxHeads * 8];
+  PlanStage<kPlanMaxHeads> in;
   int64_t pair_total[1024];  // (chunk, head) pairs: launch_plan bounds them at 1024
 };
-
-// Candidate j of (chunk c, head h): kind, slot in layer, length, t_raw,
-// t_remap; false when the candidate is not a segment.
-__device__ __forceinline__ bool plan_candidate(const PlanArgs& a, const PlanSmem& sm, int c,
-                                               int h, int j, int& kind, int& slot, int& len,
-                                               int64_t& traw, int64_t& tremap) {
-  const HeadState& s = sm.st[h];
-  const int64_t ct = chunk_time(a, c);
-  const int64_t sync_t = map_sink_time(ct, a.sink_mode, a.cmin, a.cmax, a.lag);
-  const int thr = s.sink_capacity;
-  if (j < kCandSink) {
-    const int nsr = static_cast<int>(sm.vc[h * 3 + 0]);
-    const int ns = (thr > 0 && thr < nsr) ? thr : nsr;
-    if (j >= ns || j >= a.max_sink) return false;
-    kind = kDstSink;
-    slot = h * a.max_sink + j;
-    len = a.F;
-    traw = j;
-    tremap = sync_t;
-    return true;
-  }
-  j -= kCandSink;
-  if (j < kCandRecent) {
-    const int nr = static_cast<int>(sm.vc[h * 3 + 2]);
-    if (j >= nr || j >= a.max_recent) return false;
-    kind = kDstRecent;
-    slot = h * a.max_recent + j;
-    len = a.F;
-    traw = tremap = -1;
-    return true;
-  }
-  j -= kCandRecent;
-  if (j < kCandMiddle) {
-    if (s.kind == kCyclic) {
-      const int period = s.period > 0 ? s.period : 1;
-      const int bcap = s.bucket_cap > 0 ? s.bucket_cap : 1;
-      const int phase = static_cast<int>(((ct % period) + period) % period);
-      const int pb = phase * kMaxBucket;
-      const int pe = pb + (bcap < kMaxBucket ? bcap : kMaxBucket);
-      if (j < pb || j >= pe || j >= kMaxPhase * kMaxBucket) return false;
-      if (s.cyclic_slot[j] < 0 || s.cyclic_t[j] < thr) return false;
-      kind = kDstMiddle;
-      slot = h * a.max_middle + j;
-      len = a.F;
-      traw = s.cyclic_t[j];
-      tremap = sync_t;
-      return true;
-    }
-    if (s.kind == kStride || s.kind == kLag) {
-      if (j >= s.tkey_count || j >= kMaxTKeyed) return false;
-      if (s.tkey_t[j] < thr) return false;
-      kind = kDstMiddle;
-      slot = h * a.max_middle + j;
-      len = a.F;
-      traw = s.tkey_t[j];
-      tremap = s.kind == kStride ? sync_t : int64_t(-1);
-      return true;
-    }
-    return false;
-  }
-  j -= kCandMiddle;
-  if (s.kind != kMerge || j >= s.done_count || j >= kMaxMergeBlocks) return false;
-  const int bs = s.done_slot[j];
-  if (bs < 0 || bs >= a.mmb || s.done_start_t[j] <= 0) return false;
-  const int32_t tok = sm.mtc[h * a.mmb + bs];
-  if (tok <= 0) return false;
-  kind = kSrcMerge;
-  slot = h * a.mmb + bs;
-  len = tok;
-  traw = 0;
-  tremap = s.done_median_t[j];
-  return true;
-}
 
 __global__ void __launch_bounds__(kPlanWarpThreads, 1) plan_warp_kernel(PlanArgs a) {
   extern __shared__ __align__(16) uint8_t plan_smem_raw[];
@@ -307,15 +184,7 @@ __global__ void __launch_bounds__(kPlanWarpThreads, 1) plan_warp_kernel(PlanArgs
   const int nwarps = blockDim.x >> 5;
   const int npair = a.C * a.H;
   // stage this layer's records, valid counts and merge token counts
-  {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.states);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(sm.st);
-    for (int i = tid; i < a.H * int(sizeof(HeadState) / 4); i += blockDim.x) dst[i] = src[i];
-    const int64_t* vcl = a.vc + int64_t(a.layer) * a.H * 3;
-    for (int i = tid; i < a.H * 3; i += blockDim.x) sm.vc[i] = vcl[i];
-    const int32_t* ml = a.mtc + int64_t(a.layer) * a.H * a.mmb;
-    for (int i = tid; i < a.H * a.mmb; i += blockDim.x) sm.mtc[i] = ml[i];
-  }
+  stage_plan_inputs(sm.in, a, tid, blockDim.x);
   __syncthreads();
   // pass 1: each (chunk, head)'s token total
   for (int pr = warp; pr < npair; pr += nwarps) {
@@ -325,7 +194,7 @@ __global__ void __launch_bounds__(kPlanWarpThreads, 1) plan_warp_kernel(PlanArgs
       const int j = j0 + lane;
       int kind = 0, slot = 0, len = 0;
       int64_t traw = 0, tremap = 0;
-      const bool v = j < kCand && plan_candidate(a, sm, c, h, j, kind, slot, len, traw, tremap);
+      const bool v = j < kCand && plan_candidate(a, sm.in, c, h, j, kind, slot, len, traw, tremap);
       const uint32_t bal = __ballot_sync(0xffffffffu, v);
       const int fp = fp_base + __popc(bal & ((1u << lane) - 1u));
       tot += (v && fp < a.S) ? len : 0;
@@ -376,7 +245,7 @@ __global__ void __launch_bounds__(kPlanWarpThreads, 1) plan_warp_kernel(PlanArgs
       const int j = j0 + lane;
       int kind = 0, slot = 0, len = 0;
       int64_t traw = 0, tremap = 0;
-      const bool v = j < kCand && plan_candidate(a, sm, c, h, j, kind, slot, len, traw, tremap);
+      const bool v = j < kCand && plan_candidate(a, sm.in, c, h, j, kind, slot, len, traw, tremap);
       const uint32_t bal = __ballot_sync(0xffffffffu, v);
       const int fp = fp_base + __popc(bal & ((1u << lane) - 1u));
       const bool emit = v && fp < a.S;
@@ -389,14 +258,7 @@ __global__ void __launch_bounds__(kPlanWarpThreads, 1) plan_warp_kernel(PlanArgs
       }
       if (emit) {
         const int jj = base + fp;
-        int32_t sg = slot;
-        if (a.add_layer_offset) {
-          const int per_head = kind == kDstSink     ? a.max_sink
-                               : kind == kDstMiddle ? a.max_middle
-                               : kind == kDstRecent ? a.max_recent
-                                                    : a.mmb;
-          sg += a.layer * a.H * per_head;
-        }
+        const int32_t sg = a.add_layer_offset ? layer_slot(a, kind, slot) : slot;
         a.sk[jj] = kind;
         a.sg[jj] = sg;
         a.sl[jj] = len;
@@ -433,38 +295,14 @@ int launch_plan(const pkv_cache_t* c, const uint8_t* states_layer, int layer,
   if (layer < 0 || layer >= c->num_layers) return PKV_EINVAL;
   const int n = num_chunks * c->num_heads;
   if (n > 1024) return PKV_ECAPACITY;
-  PlanArgs a{};
-  a.vc = c->valid_count;
-  a.mtc = c->merge_token_count;
-  a.states = reinterpret_cast<const HeadState*>(states_layer);
-  a.layer = layer;
-  a.H = c->num_heads;
-  a.F = c->frame_seqlen;
-  a.max_sink = c->max_sink;
-  a.max_middle = c->max_middle;
-  a.max_recent = c->max_recent;
-  a.mmb = c->max_merge_blocks;
-  a.S = int(plan_segments_per_head(c));
-  a.C = num_chunks;
-  a.sink_mode = sink_mode;
-  a.cmin = cmin;
-  a.cmax = cmax;
-  a.lag = lag;
-  a.add_layer_offset = add_layer_offset;
-  a.check_capacity = check_capacity;
-  a.capacity = c->max_pack_tokens;
-  for (int i = 0; i < num_chunks; ++i) a.t[i] = current_t[i];
-  a.t_dev = t_dev;
-  a.cu = cu;
+  PlanArgs a = plan_args(c, states_layer, layer, current_t, num_chunks, sink_mode, cmin, cmax,
+                         lag, check_capacity, add_layer_offset, cu, total, counter, t_dev);
   a.sk = sk;
   a.sg = sg;
   a.sl = sl;
   a.dst = dst;
   a.traw = traw;
   a.tremap = tremap;
-  a.total_out = total;
-  a.counter = counter;
-  a.status = c->status;
   // the warp planner covers the pool bounds its candidate list enumerates;
   // other shapes take the thread-per-(chunk, head) walk
   if (a.H <= kPlanMaxHeads && a.max_sink <= kCandSink && a.max_recent <= kCandRecent &&

@@ -115,3 +115,19 @@ def test_update_rejects_bad_shapes(cuda):
                      torch.zeros(1, 104, 2, 128, device=cuda, dtype=torch.bfloat16), 0,
                      cache_update_mode="other")
     assert int(caches[0].ctx.mgr.valid_count().abs().sum()) == 0
+
+
+def test_megacache_two_launch_plan_pack(cuda):
+    """The same blocks with the planner and the pack as two launches
+    (PKV_FUSED_PLAN_PACK=0; the default pack plans for itself)."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, PKV_FUSED_PLAN_PACK="0")
+    here = os.path.dirname(os.path.abspath(__file__))
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p",
+                        "no:cacheprovider", os.path.join(here, "test_gpu_megacache.py"),
+                        "-k", "blocks_match_oracle and baseline"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert " passed" in r.stdout
