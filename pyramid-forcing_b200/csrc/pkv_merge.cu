@@ -284,6 +284,250 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch m) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// merge_grid_kernel: the same accumulation when token positions come from the
+// frame grid (t -> y = t / W, x = t % W; the MegaCache path).  A group's
+// tokens are then a closed form: rows py*ps .. py*ps+ps-1, columns
+// px*ps .. px*ps+ps-1 of the grid, enumerated row by row, which is ascending
+// token order; no per-launch token lists.  One warp owns one group of one
+// head for the whole launch and keeps its fp32 sums in registers across the
+// frames (lane = 4 dims of head_dim 128), flushing them to the accumulator
+// rows when the frame's slot changes and at the end.  Heads whose grid does
+// not fit the closed form (patch size <= 0, or more groups than MTPA, where
+// the reference folds the excess tokens into group 0) take a warp-wide scan
+// of the frame's tokens, still in ascending order.
+// ---------------------------------------------------------------------------
+constexpr int kGridGroupsPerCta = 8;  // one warp per group
+constexpr int kGridThreads = kGridGroupsPerCta * 32;
+
+struct MergeGrid {
+  int W, pc, sng, ps;
+  bool closed;
+  __device__ __forceinline__ int gid(int t) const {
+    const int y = t / W, x = t - y * W;
+    int g = ps > 0 ? (y / ps) * pc + x / ps : 0;
+    return (g < 0 || g >= sng) ? 0 : g;
+  }
+};
+
+// Token i (< ps * ps) of group g in the closed form, or -1 outside the frame.
+__device__ __forceinline__ int grid_token(const MergeGrid& G, int FSEQ, int g, int i) {
+  const int py = g / G.pc, px = g - py * G.pc;
+  const int dy = i / G.ps, dx = i - dy * G.ps;
+  const int y = py * G.ps + dy, x = px * G.ps + dx;
+  if (x >= G.W) return -1;
+  const int t = y * G.W + x;
+  return t < FSEQ ? t : -1;
+}
+
+__device__ __forceinline__ void add_row(float (&sk)[4], float (&sv)[4], uint2 kr, uint2 vr) {
+  const uint32_t kw[2] = {kr.x, kr.y}, vw[2] = {vr.x, vr.y};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t kb = (e & 1) ? (kw[e >> 1] >> 16) : (kw[e >> 1] & 0xffffu);
+    const uint32_t vb = (e & 1) ? (vw[e >> 1] >> 16) : (vw[e >> 1] & 0xffffu);
+    sk[e] = __fadd_rn(sk[e], bf16_bits_to_f32(kb));
+    sv[e] = __fadd_rn(sv[e], bf16_bits_to_f32(vb));
+  }
+}
+
+__device__ __forceinline__ void store_acc(const MergeLaunch& m, int64_t row, int d0,
+                                          const float (&sk)[4], const float (&sv)[4]) {
+  *reinterpret_cast<float4*>(m.acc_k + row * 128 + d0) = make_float4(sk[0], sk[1], sk[2], sk[3]);
+  *reinterpret_cast<float4*>(m.acc_v + row * 128 + d0) = make_float4(sv[0], sv[1], sv[2], sv[3]);
+}
+
+constexpr int kMergeBatch = 3;     // frames whose rows are loaded together (a block's 3)
+constexpr int kMergeBatchTok = 4;  // tokens per group in the prefetched form (patch 2 x 2)
+
+__global__ void __launch_bounds__(kGridThreads, 2) merge_grid_kernel(MergeLaunch m) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, tile = blockIdx.y;
+  const int g = tile * kGridGroupsPerCta + warp;
+  const int FSEQ = m.FSEQ, MMA = m.MMA, MTPA = m.MTPA;
+  const int32_t bf = m.states[h].block_frames;
+  MergeGrid G;
+  G.W = m.pos_width;
+  G.ps = m.states[h].patch_size;
+  // the frame's spatial extent: max x and max y over its tokens
+  const int mx = (G.W < FSEQ ? G.W : FSEQ) - 1, my = (FSEQ - 1) / G.W;
+  G.pc = G.ps > 0 ? mx / G.ps + 1 : 1;
+  const int pr = G.ps > 0 ? my / G.ps + 1 : 1;
+  const int ng = pr * G.pc;
+  G.sng = ng > MTPA ? MTPA : ng;
+  G.closed = G.ps > 0 && ng <= MTPA;
+  const int d0 = lane * 4;
+  // the group's tokens are the same in every frame: with at most 4 of them
+  // (patch 2 x 2) a batch of frames' rows is loaded at once
+  const bool pre = G.closed && G.ps * G.ps <= kMergeBatchTok && g < MTPA;
+  int tt[kMergeBatchTok];
+  int ntok = 0;
+#pragma unroll
+  for (int i = 0; i < kMergeBatchTok; ++i) {
+    tt[i] = pre && i < G.ps * G.ps ? grid_token(G, FSEQ, g, i) : -1;
+    ntok += tt[i] >= 0;
+  }
+  int cur = -1;  // accumulator slot whose sums the registers hold
+  float sk[4] = {0.f, 0.f, 0.f, 0.f}, sv[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int f0 = 0; f0 < m.F; f0 += kMergeBatch) {
+    // ---- this batch's descriptors, then (prefetched form) its rows
+    int32_t kind[kMergeBatch], slot[kMergeBatch], fresh[kMergeBatch], fin[kMergeBatch];
+#pragma unroll
+    for (int b = 0; b < kMergeBatch; ++b) {
+      kind[b] = -1;
+      slot[b] = fresh[b] = 0;
+      fin[b] = -1;
+      if (f0 + b < m.F) {
+        const int di = h * m.F + f0 + b;
+        kind[b] = m.dkind[di];
+        slot[b] = m.dslot[di];
+        fresh[b] = m.dnew[di];
+        fin[b] = m.dfin[di];
+      }
+    }
+    uint2 kr[kMergeBatch][kMergeBatchTok], vr[kMergeBatch][kMergeBatchTok];
+    float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pv = pk;
+    int pslot = -1;  // slot whose accumulator rows pk / pv hold
+    if (pre) {
+#pragma unroll
+      for (int b = 0; b < kMergeBatch; ++b) {
+        if (kind[b] != kDstMergeAccum || slot[b] < 0 || slot[b] >= MMA) continue;
+        const int64_t fo = int64_t(f0 + b) * m.frame_stride + int64_t(h) * m.head_stride;
+#pragma unroll
+        for (int i = 0; i < kMergeBatchTok; ++i) {
+          if (tt[i] < 0) continue;
+          kr[b][i] = *reinterpret_cast<const uint2*>(m.new_k + fo + int64_t(tt[i]) * m.tok_stride + d0);
+          vr[b][i] = *reinterpret_cast<const uint2*>(m.new_v + fo + int64_t(tt[i]) * m.tok_stride + d0);
+        }
+      }
+      // the first merge frame's accumulator rows, when it continues a block
+#pragma unroll
+      for (int b = kMergeBatch - 1; b >= 0; --b) {
+        if (kind[b] == kDstMergeAccum && slot[b] >= 0 && slot[b] < MMA) pslot = fresh[b] ? -1 : slot[b];
+      }
+      if (pslot >= 0 && pslot != cur) {
+        const int64_t row = (int64_t(h) * MMA + pslot) * MTPA + g;
+        pk = *reinterpret_cast<const float4*>(m.acc_k + row * 128 + d0);
+        pv = *reinterpret_cast<const float4*>(m.acc_v + row * 128 + d0);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kMergeBatch; ++b) {
+      const int f = f0 + b;
+      const int32_t a = slot[b];
+      if (kind[b] != kDstMergeAccum || a < 0) continue;  // uniform across the CTA
+      if (a >= MMA || fin[b] >= m.MMB) {
+        if (threadIdx.x == 0 && tile == 0) flag(m.status, PKV_ST_SLOT_RANGE);
+        continue;
+      }
+      const int64_t arow = (int64_t(h) * MMA + a) * MTPA;
+      if (fresh[b]) {
+        // new block: group bookkeeping visible to later launches and the accessors
+        if (tile == 0) {
+          int32_t* ggid = m.acc_gid + (int64_t(h) * MMA + a) * FSEQ;
+          for (int t = threadIdx.x; t < FSEQ; t += kGridThreads) ggid[t] = G.gid(t);
+          if (threadIdx.x == 0) m.acc_ng[h * MMA + a] = G.sng;
+        }
+        if (g < G.sng && lane == 0) {
+          const int64_t pt0 = (m.t_dev != nullptr ? __ldg(m.t_dev) : m.first_t) + f;
+          int64_t* gp = m.acc_pos + (arow + g) * 3;
+          gp[0] = pt0;
+          gp[1] = int64_t(g / G.pc) * G.ps;
+          gp[2] = int64_t(g % G.pc) * G.ps;
+        }
+      }
+      if (g >= MTPA) continue;  // warp-uniform
+      if (a != cur) {
+        if (cur >= 0) {
+          store_acc(m, (int64_t(h) * MMA + cur) * MTPA + g, d0, sk, sv);
+          if (cur == pslot) pslot = -1;  // the prefetched rows are stale now
+        }
+        cur = a;
+        if (fresh[b]) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sk[e] = sv[e] = 0.0f;
+        } else {
+          float4 k4 = pk, v4 = pv;
+          if (a != pslot) {
+            k4 = *reinterpret_cast<const float4*>(m.acc_k + (arow + g) * 128 + d0);
+            v4 = *reinterpret_cast<const float4*>(m.acc_v + (arow + g) * 128 + d0);
+          }
+          sk[0] = k4.x; sk[1] = k4.y; sk[2] = k4.z; sk[3] = k4.w;
+          sv[0] = v4.x; sv[1] = v4.y; sv[2] = v4.z; sv[3] = v4.w;
+        }
+      } else if (fresh[b]) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sk[e] = sv[e] = 0.0f;
+      }
+      int count = 0;  // the group's tokens in this frame
+      if (pre) {
+#pragma unroll
+        for (int i = 0; i < kMergeBatchTok; ++i)
+          if (tt[i] >= 0) add_row(sk, sv, kr[b][i], vr[b][i]);
+        count = ntok;
+      } else {
+        const uint16_t* kbase = m.new_k + int64_t(f) * m.frame_stride + int64_t(h) * m.head_stride;
+        const uint16_t* vbase = m.new_v + int64_t(f) * m.frame_stride + int64_t(h) * m.head_stride;
+        if (G.closed) {
+          const int n = G.ps * G.ps;
+          for (int i0 = 0; i0 < n; i0 += 8) {
+            uint2 kb[8], vb[8];
+            int tb[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              tb[j] = i0 + j < n ? grid_token(G, FSEQ, g, i0 + j) : -1;
+              if (tb[j] >= 0) {
+                kb[j] = *reinterpret_cast<const uint2*>(kbase + int64_t(tb[j]) * m.tok_stride + d0);
+                vb[j] = *reinterpret_cast<const uint2*>(vbase + int64_t(tb[j]) * m.tok_stride + d0);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (tb[j] >= 0) {
+                add_row(sk, sv, kb[j], vb[j]);
+                ++count;
+              }
+            }
+          }
+        } else if (g < G.sng) {
+          for (int base = 0; base < FSEQ; base += 32) {
+            const int t = base + lane;
+            unsigned mine = __ballot_sync(0xffffffffu, t < FSEQ && G.gid(t) == g);
+            count += __popc(mine);
+            while (mine) {
+              const int tk = base + __ffs(mine) - 1;
+              mine &= mine - 1;
+              const uint2 kx = *reinterpret_cast<const uint2*>(kbase + int64_t(tk) * m.tok_stride + d0);
+              const uint2 vx = *reinterpret_cast<const uint2*>(vbase + int64_t(tk) * m.tok_stride + d0);
+              add_row(sk, sv, kx, vx);
+            }
+          }
+        }
+      }
+      if (fresh[b] && lane == 0)  // divisor = token count * block_frames (zero past the groups)
+        m.acc_tpg[arow + g] = g < G.sng ? static_cast<float>(count) * static_cast<float>(bf) : 0.0f;
+      if (fin[b] >= 0 && g < G.sng) {
+        // every frame of a block has the same grid, so this frame's count gives
+        // the block's divisor
+        const float divisor = static_cast<float>(count) * static_cast<float>(bf);
+        const float inv = divisor > 0.0f ? __frcp_rn(divisor) : 0.0f;
+        const int64_t prow = (int64_t(h) * m.MMB + fin[b]) * MTPA + g;
+        uint2 ok, ov;
+        ok.x = f32_to_bf16_bits(__fmul_rn(sk[0], inv)) | (f32_to_bf16_bits(__fmul_rn(sk[1], inv)) << 16);
+        ok.y = f32_to_bf16_bits(__fmul_rn(sk[2], inv)) | (f32_to_bf16_bits(__fmul_rn(sk[3], inv)) << 16);
+        ov.x = f32_to_bf16_bits(__fmul_rn(sv[0], inv)) | (f32_to_bf16_bits(__fmul_rn(sv[1], inv)) << 16);
+        ov.y = f32_to_bf16_bits(__fmul_rn(sv[2], inv)) | (f32_to_bf16_bits(__fmul_rn(sv[3], inv)) << 16);
+        *reinterpret_cast<uint2*>(m.mk + prow * 128 + d0) = ok;
+        *reinterpret_cast<uint2*>(m.mv + prow * 128 + d0) = ov;
+        __syncwarp();  // lane 0's group position of a block begun in this launch
+        if (lane < 3) m.mpos[prow * 3 + lane] = m.acc_pos[(arow + g) * 3 + lane];
+        if (g == 0 && lane == 0) m.mtc[h * m.MMB + fin[b]] = G.sng;
+      }
+    }
+  }
+  if (cur >= 0 && g < MTPA) store_acc(m, (int64_t(h) * MMA + cur) * MTPA + g, d0, sk, sv);
+}
+
 int launch_merge(const MergeLaunch& m, cudaStream_t stream) {
   if (m.H == 0 || m.F == 0) return PKV_OK;
   if (m.FSEQ <= 0 || m.FSEQ > 16384 || m.MTPA <= 0 || m.MTPA > 32767 || m.D <= 0)
@@ -295,6 +539,19 @@ int launch_merge(const MergeLaunch& m, cudaStream_t stream) {
     if (cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(smem)) != cudaSuccess)
       return PKV_ELAUNCH;
+  }
+  // positions from the frame grid, head_dim 128 with 8-byte aligned rows:
+  // warp per group with the closed-form token lists
+  const bool grid_ok =
+      m.new_pos == nullptr && m.pos_width > 0 && m.D == 128 && (m.tok_stride & 3) == 0 &&
+      (m.frame_stride & 3) == 0 && (m.head_stride & 3) == 0 &&
+      ((reinterpret_cast<uintptr_t>(m.new_k) | reinterpret_cast<uintptr_t>(m.new_v)) & 7) == 0 &&
+      ((reinterpret_cast<uintptr_t>(m.acc_k) | reinterpret_cast<uintptr_t>(m.acc_v)) & 15) == 0 &&
+      ((reinterpret_cast<uintptr_t>(m.mk) | reinterpret_cast<uintptr_t>(m.mv)) & 7) == 0;
+  if (grid_ok) {
+    dim3 grid(m.H, (m.MTPA + kGridGroupsPerCta - 1) / kGridGroupsPerCta);
+    merge_grid_kernel<<<grid, kGridThreads, 0, stream>>>(m);
+    return launch_status();
   }
   dim3 grid(m.H, (m.MTPA + kGroupsPerCta - 1) / kGroupsPerCta);
   merge_kernel<<<grid, kMergeThreads, smem, stream>>>(m);

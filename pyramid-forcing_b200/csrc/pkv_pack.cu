@@ -176,24 +176,13 @@ __global__ void __launch_bounds__(256) pack_kernel(PackArgs a) {
 constexpr int kPack128MaxSeg = 2048;  // plans with more segments use pack_kernel
 
 // ---------------------------------------------------------------------------
-// pack_bulk_kernel (head_dim 128): tiles of 64 tokens staged through shared
-// memory by bulk async copies.  One thread per block keeps a 2-stage ring of
-// (K, V, positions) tiles in flight with cp.async.bulk global -> shared (a
-// plain per-block copy); V goes straight back out with a bulk shared -> global store; the
-// block's threads read K (and positions) from shared memory, rotate and store
-// K and copy the positions.  A block holds up to 2 x 33.5 KB in flight without
-// spending registers on it, which a gather-copy needs to approach HBM rate.
+// Tiles of 64 tokens for the head_dim-128 pack (pack_ws_kernel below): the
+// segments are cut into tiles, the tiles listed in segment order and dealt
+// to the blocks in equal contiguous ranges.
 // ---------------------------------------------------------------------------
 constexpr int kBulkTok = 64;
-constexpr int kBulkStages = 2;
-constexpr int kBulkThreads = 256;
 constexpr uint64_t kBulkTimeoutNs = 4000000000ull;
 
-struct __align__(128) BulkStage {
-  uint16_t k[kBulkTok * 128];
-  uint16_t v[kBulkTok * 128];
-  int64_t pos[kBulkTok * 3];
-};
 struct BulkTileMeta {
   int64_t dst0;      // packed row of the segment's first token
   int64_t src_row;   // pool row of the tile's first token
@@ -201,13 +190,6 @@ struct BulkTileMeta {
   int tok0, ntok, kind;
   int bad;           // segment failed its bounds checks: skip
   int pos_in_smem;   // positions arrived with the bulk copy
-};
-struct BulkSmem {
-  BulkStage st[kBulkStages];
-  uint64_t full[kBulkStages];
-  BulkTileMeta meta[kBulkStages];
-  int tile_start[kPack128MaxSeg + 1];
-  int warp_tot[kBulkThreads / 32];
 };
 
 // The pack that plans for itself (the path MegaCache.attend takes): the
@@ -228,10 +210,8 @@ struct PlannedSmem {
   int64_t pair_sync[kPlanPackMaxPairs];
   int pair_phase[kPlanPackMaxPairs];
   int64_t median[kPlanPackMaxHeads * kCandMerge];
-  int warp_tok[kBulkThreads / 32];
+  int warp_tok[32];
 };
-static_assert(sizeof(PlanStage<kPlanPackMaxHeads>) <= sizeof(BulkStage) * kBulkStages,
-              "the planner inputs fit the stage buffers");
 
 // Row r of a table with `rows` rows, clamped into [0, rows) (rows >= 1).
 __device__ __forceinline__ int clamp_row(int64_t r, int rows) {
@@ -284,17 +264,20 @@ __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// The tile list both pack kernels share.  Every thread of the block takes
+// part; on return (after a block barrier) tile_start[j] is the first tile of
+// segment j and tile_start[n] the total, and with kPlanned the candidates'
+// descriptors and packed rows are in `ps` and block 0 has written
+// cu_seqlens_k, the token total and the counter.  The planner inputs borrow
+// `stage_mem` (>= sizeof(PlanStage<kPlanPackMaxHeads>)) until then.
 // kPlanned: the segments are the planner's candidates (pkv_plan.cuh), which
-// every block evaluates itself from the staged state records; block 0 writes
-// cu_seqlens_k, the token total and the counter.  Otherwise they come from a
-// plan in global memory (sk / sg / sl / dst / tremap).
+// every block evaluates itself from the staged state records.  Otherwise
+// they come from a plan in global memory (sk / sg / sl / dst / tremap).
+// ---------------------------------------------------------------------------
 template <bool kPlanned>
-__global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, PlanArgs pa) {
-  extern __shared__ uint8_t pk_raw[];
-  BulkSmem& sm = *reinterpret_cast<BulkSmem*>(
-      (reinterpret_cast<uintptr_t>(pk_raw) + 127) & ~uintptr_t(127));
-  PlannedSmem& ps = *reinterpret_cast<PlannedSmem*>(
-      (reinterpret_cast<uintptr_t>(pk_raw) + 127 + sizeof(BulkSmem) + 127) & ~uintptr_t(127));
+__device__ int pack_tile_list(const PackArgs& a, const PlanArgs& pa, int* tile_start,
+                              int* warp_tot, PlannedSmem& ps, void* stage_mem) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n = kPlanned ? pa.C * pa.H * kCand : a.n_seg;
   const int per = (n + blockDim.x - 1) / blockDim.x;
@@ -303,7 +286,7 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
   if (kPlanned) {
     // ---- plan: every candidate's descriptor and length, in place of the
     // planner's descriptor arrays
-    PlanStage<kPlanPackMaxHeads>& in = *reinterpret_cast<PlanStage<kPlanPackMaxHeads>*>(sm.st);
+    PlanStage<kPlanPackMaxHeads>& in = *reinterpret_cast<PlanStage<kPlanPackMaxHeads>*>(stage_mem);
     stage_plan_inputs(in, pa, threadIdx.x, blockDim.x);
     __syncthreads();
     for (int pr = threadIdx.x; pr < pa.C * pa.H; pr += blockDim.x) {
@@ -328,7 +311,7 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
                         uint32_t(len > 0 ? layer_slot(pa, kind, slot) : 0);
       ps.cand_off[j] = len;  // the length until the scan below
       const int nt = (len + kBulkTok - 1) / kBulkTok;
-      sm.tile_start[j] = nt;
+      tile_start[j] = nt;
       run += nt;
       tok += len;
     }
@@ -347,7 +330,7 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
           nt = (len + kBulkTok - 1) / kBulkTok;
         }
       }
-      sm.tile_start[sg] = nt;
+      tile_start[sg] = nt;
       run += nt;
     }
   }
@@ -362,19 +345,14 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
     }
   }
   if (lane == 31) {
-    sm.warp_tot[warp] = incl;
+    warp_tot[warp] = incl;
     if (kPlanned) ps.warp_tok[warp] = tincl;
-  }
-  if (threadIdx.x == 0) {
-    for (int st = 0; st < kBulkStages; ++st)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(pk_smem(&sm.full[st])));
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   int before = 0, total = 0, tbefore = 0, ttotal = 0;
   for (int w = 0; w < int(blockDim.x >> 5); ++w) {
-    if (w < warp) before += sm.warp_tot[w];
-    total += sm.warp_tot[w];
+    if (w < warp) before += warp_tot[w];
+    total += warp_tot[w];
     if (kPlanned) {
       if (w < warp) tbefore += ps.warp_tok[w];
       ttotal += ps.warp_tok[w];
@@ -382,8 +360,8 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
   }
   int acc = before + incl - run, tacc = tbefore + tincl - tok;
   for (int sg = s_begin; sg < s_end; ++sg) {
-    const int nt = sm.tile_start[sg];
-    sm.tile_start[sg] = acc;
+    const int nt = tile_start[sg];
+    tile_start[sg] = acc;
     acc += nt;
     if (kPlanned) {
       const int len = ps.cand_off[sg];
@@ -392,7 +370,7 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
     }
   }
   if (threadIdx.x == 0) {
-    sm.tile_start[n] = total;
+    tile_start[n] = total;
     if (kPlanned) ps.cand_off[n] = ttotal;
   }
   __syncthreads();
@@ -409,82 +387,233 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
     }
   }
 
+  return total;
+}
+
+struct PackTile {
+  int64_t dst0;     // packed row of the segment's first token
+  int64_t src_row;  // pool row of the tile's first token
+  int64_t tm;       // remapped time (>= 0) or -1
+  int tok0, ntok, kind, len;
+  int bad;          // segment failed its bounds checks: skip
+};
+
+// Tile u of the list; `iseg` is the walker's segment cursor (tiles visited in
+// increasing order).  A bad segment's first tile sets the status bit.
+template <bool kPlanned>
+__device__ __forceinline__ PackTile pack_tile(const PackArgs& a, const PlanArgs& pa,
+                                              const int* tile_start, const PlannedSmem& ps,
+                                              int& iseg, int u) {
+  while (tile_start[iseg + 1] <= u) ++iseg;
+  int kind, len;
+  int64_t slot, dst0, seg_tremap;
+  if (kPlanned) {
+    const uint32_t d = ps.cand_desc[iseg];
+    kind = int(d >> 28);
+    slot = int64_t(d & ((1u << kDescSlotBits) - 1u));
+    dst0 = ps.cand_off[iseg];
+    len = ps.cand_off[iseg + 1] - ps.cand_off[iseg];
+    const uint32_t src = (d >> kDescSlotBits) & 3u;
+    const int pr = iseg / kCand;
+    seg_tremap = src == kRemapSync ? ps.pair_sync[pr]
+                 : src == kRemapMedian
+                     ? ps.median[(pr % pa.H) * kCandMerge + iseg - pr * kCand -
+                                 (kCandSink + kCandRecent + kCandMiddle)]
+                     : int64_t(-1);
+  } else {
+    kind = a.sk[iseg];
+    len = a.sl[iseg];
+    slot = a.sg[iseg];
+    dst0 = a.dst[iseg];
+    seg_tremap = a.tremap != nullptr ? a.tremap[iseg] : -1;
+  }
+  PackTile t;
+  const int stride_tok = kind == kSrcMerge ? a.MTPA : a.F;
+  t.kind = kind;
+  t.len = len;
+  t.tok0 = (u - tile_start[iseg]) * kBulkTok;
+  t.ntok = min(kBulkTok, len - t.tok0);
+  t.dst0 = dst0;
+  t.bad = slot < 0 || slot >= a.rows[kind] || len > stride_tok || dst0 < 0 ||
+          dst0 + len > a.out_rows || a.k[kind] == nullptr;
+  t.src_row = slot * stride_tok + t.tok0;
+  t.tm = (a.rope && a.pos[kind] != nullptr) ? seg_tremap : -1;
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// pack_ws_kernel (head_dim 128): one block per SM, the roles split over
+// warps.  Warp 0 keeps a 4-stage ring of K (+ positions) tiles loading with
+// cp.async.bulk global -> shared (a plain per-block copy); warp 1 moves V on
+// a 5-stage ring of its own (bulk load, then bulk store straight back out,
+// the slot reused once the store has read it), which no other warp waits
+// on; warps 2..17 rotate and store K and copy the positions, releasing each
+// K stage through an mbarrier instead of a block barrier.  Up to 9 tiles
+// (150 KB) per SM stay in flight without spending registers on them; the
+// earlier design (two blocks per SM, each refilling one 2-stage K+V ring
+// only after a block barrier) kept about one tile per block in flight.
+// ---------------------------------------------------------------------------
+constexpr int kWsKStages = 4;
+constexpr int kWsVStages = 5;
+constexpr int kWsConsumers = 512;  // 16 warps
+constexpr int kWsThreads = kWsConsumers + 64;
+
+struct __align__(128) WsKStage {
+  uint16_t k[kBulkTok * 128];
+  int64_t pos[kBulkTok * 3];
+};
+struct __align__(128) WsVStage {
+  uint16_t v[kBulkTok * 128];
+};
+struct WsVMeta {
+  int64_t drow;  // packed row of the tile's first token
+  int ntok, bad;
+};
+struct WsSmem {
+  WsKStage ks[kWsKStages];
+  WsVStage vs[kWsVStages];
+  uint64_t kfull[kWsKStages], kempty[kWsKStages], vfull[kWsVStages];
+  BulkTileMeta meta[kWsKStages];
+  WsVMeta vmeta[kWsVStages];
+  int tile_start[kPack128MaxSeg + 1];
+  int warp_tot[32];
+};
+static_assert(sizeof(PlanStage<kPlanPackMaxHeads>) <= sizeof(WsKStage) * kWsKStages,
+              "the planner inputs fit the K stage buffers");
+
+__device__ __forceinline__ void pk_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pk_smem(b)) : "memory");
+}
+__device__ __forceinline__ void pk_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(pk_smem(b)),
+               "r"(bytes)
+               : "memory");
+}
+
+template <bool kPlanned>
+__global__ void __launch_bounds__(kWsThreads, 1) pack_ws_kernel(PackArgs a, PlanArgs pa) {
+  extern __shared__ uint8_t pk_raw[];
+  WsSmem& sm = *reinterpret_cast<WsSmem*>(
+      (reinterpret_cast<uintptr_t>(pk_raw) + 127) & ~uintptr_t(127));
+  PlannedSmem& ps = *reinterpret_cast<PlannedSmem*>(
+      (reinterpret_cast<uintptr_t>(pk_raw) + 127 + sizeof(WsSmem) + 127) & ~uintptr_t(127));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kWsKStages; ++st) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(pk_smem(&sm.kfull[st])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(pk_smem(&sm.kempty[st])),
+                   "r"(kWsConsumers / 32));
+    }
+    for (int st = 0; st < kWsVStages; ++st)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(pk_smem(&sm.vfull[st])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  const int n = kPlanned ? pa.C * pa.H * kCand : a.n_seg;
+  const int total = pack_tile_list<kPlanned>(a, pa, sm.tile_start, sm.warp_tot, ps, sm.ks);
   const int per_block = (total + int(gridDim.x) - 1) / int(gridDim.x);
   const int u_begin = min(total, int(blockIdx.x) * per_block);
   const int count = min(total, u_begin + per_block) - u_begin;
   if (count <= 0) return;
-
-  // ---- producer (thread 0): tile i -> stage i % kBulkStages
-  int iseg = 0;
-  if (threadIdx.x == 0) {
-    int lo = 0, hi = n;  // tile_start[lo] <= u_begin < tile_start[hi]
+  // segment of the block's first tile: tile_start[lo] <= u_begin < tile_start[lo + 1]
+  auto first_seg = [&]() {
+    int lo = 0, hi = n;
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
       if (sm.tile_start[mid] <= u_begin) lo = mid; else hi = mid;
     }
-    iseg = lo;
-  }
-  auto issue = [&](int i) {
-    const int u = u_begin + i;
-    while (sm.tile_start[iseg + 1] <= u) ++iseg;
-    const int st = i % kBulkStages;
-    BulkTileMeta& m = sm.meta[st];
-    int kind, len;
-    int64_t slot, dst0, seg_tremap;
-    if (kPlanned) {
-      const uint32_t d = ps.cand_desc[iseg];
-      kind = int(d >> 28);
-      slot = int64_t(d & ((1u << kDescSlotBits) - 1u));
-      dst0 = ps.cand_off[iseg];
-      len = ps.cand_off[iseg + 1] - ps.cand_off[iseg];
-      const uint32_t src = (d >> kDescSlotBits) & 3u;
-      const int pr = iseg / kCand;
-      seg_tremap = src == kRemapSync ? ps.pair_sync[pr]
-                   : src == kRemapMedian
-                       ? ps.median[(pr % pa.H) * kCandMerge + iseg - pr * kCand -
-                                   (kCandSink + kCandRecent + kCandMiddle)]
-                       : int64_t(-1);
-    } else {
-      kind = a.sk[iseg];
-      len = a.sl[iseg];
-      slot = a.sg[iseg];
-      dst0 = a.dst[iseg];
-      seg_tremap = a.tremap != nullptr ? a.tremap[iseg] : -1;
-    }
-    const int stride_tok = kind == kSrcMerge ? a.MTPA : a.F;
-    const int tok0 = (u - sm.tile_start[iseg]) * kBulkTok;
-    m.kind = kind;
-    m.tok0 = tok0;
-    m.ntok = min(kBulkTok, len - tok0);
-    m.dst0 = dst0;
-    m.bad = slot < 0 || slot >= a.rows[kind] || len > stride_tok || dst0 < 0 ||
-            dst0 + len > a.out_rows || a.k[kind] == nullptr;
-    uint64_t* bar = &sm.full[st];
-    if (m.bad) {
-      if (tok0 == 0)
-        flag(a.status, dst0 + len > a.out_rows ? PKV_ST_PACK_OVERFLOW : PKV_ST_SLOT_RANGE);
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pk_smem(bar)) : "memory");
-      return;
-    }
-    m.src_row = slot * stride_tok + tok0;
-    m.tm = (a.rope && a.pos[kind] != nullptr) ? seg_tremap : -1;
-    // 16-byte rule of the bulk copy: 24 * src_row and 24 * ntok must be multiples of 16
-    m.pos_in_smem = a.pos[kind] != nullptr && (m.src_row & 1) == 0 && (m.ntok & 1) == 0;
-    const uint32_t kv_bytes = uint32_t(m.ntok) * 256;
-    const uint32_t pos_bytes = m.pos_in_smem ? uint32_t(m.ntok) * 24 : 0;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(pk_smem(bar)),
-                 "r"(2 * kv_bytes + pos_bytes)
-                 : "memory");
-    bulk_g2s(sm.st[st].k, a.k[kind] + m.src_row * 128, kv_bytes, bar);
-    bulk_g2s(sm.st[st].v, a.v[kind] + m.src_row * 128, kv_bytes, bar);
-    if (pos_bytes) bulk_g2s(sm.st[st].pos, a.pos[kind] + m.src_row * 3, pos_bytes, bar);
+    return lo;
   };
-  int issued = 0;
-  if (threadIdx.x == 0)
-    for (; issued < min(kBulkStages, count); ++issued) issue(issued);
 
-  // ---- this thread's four complex pairs are fixed: resolve their tables once
-  const int ch = threadIdx.x & 15;
+  if (warp == 0) {
+    // ---- K producer
+    if (lane != 0) return;
+    int iseg = first_seg();
+    int issued = 0;
+    for (; issued < count; ++issued) {
+      const int st = issued % kWsKStages;
+      if (issued >= kWsKStages &&
+          !pk_wait(&sm.kempty[st], uint32_t(issued / kWsKStages - 1) & 1u)) {
+        flag(a.status, PKV_ST_TIMEOUT);
+        break;
+      }
+      const PackTile t = pack_tile<kPlanned>(a, pa, sm.tile_start, ps, iseg, u_begin + issued);
+      BulkTileMeta& m = sm.meta[st];
+      m.kind = t.kind;
+      m.tok0 = t.tok0;
+      m.ntok = t.ntok;
+      m.dst0 = t.dst0;
+      m.bad = t.bad;
+      m.src_row = t.src_row;
+      m.tm = t.tm;
+      if (t.bad) {
+        if (t.tok0 == 0)
+          flag(a.status, t.dst0 + t.len > a.out_rows ? PKV_ST_PACK_OVERFLOW : PKV_ST_SLOT_RANGE);
+        m.pos_in_smem = 0;
+        pk_arrive(&sm.kfull[st]);
+        continue;
+      }
+      // 16-byte rule of the bulk copy: 24 * src_row and 24 * ntok must be multiples of 16
+      m.pos_in_smem = a.pos[t.kind] != nullptr && (t.src_row & 1) == 0 && (t.ntok & 1) == 0;
+      const uint32_t k_bytes = uint32_t(t.ntok) * 256;
+      const uint32_t pos_bytes = m.pos_in_smem ? uint32_t(t.ntok) * 24 : 0;
+      pk_expect(&sm.kfull[st], k_bytes + pos_bytes);
+      bulk_g2s(sm.ks[st].k, a.k[t.kind] + t.src_row * 128, k_bytes, &sm.kfull[st]);
+      if (pos_bytes)
+        bulk_g2s(sm.ks[st].pos, a.pos[t.kind] + t.src_row * 3, pos_bytes, &sm.kfull[st]);
+    }
+    // let the loads still in flight land before the block's shared memory goes
+    for (int i = max(0, issued - kWsKStages); i < issued; ++i)
+      pk_wait(&sm.kfull[i % kWsKStages], uint32_t(i / kWsKStages) & 1u);
+    return;
+  }
+
+  if (warp == 1) {
+    // ---- V mover: load -> store, each slot reused once its store has read it
+    if (lane != 0) return;
+    int iseg = first_seg();
+    auto load = [&](int i) {
+      const int st = i % kWsVStages;
+      const PackTile t = pack_tile<kPlanned>(a, pa, sm.tile_start, ps, iseg, u_begin + i);
+      WsVMeta& vm = sm.vmeta[st];
+      vm.drow = t.dst0 + t.tok0;
+      vm.ntok = t.ntok;
+      vm.bad = t.bad;
+      if (t.bad) {
+        pk_arrive(&sm.vfull[st]);
+        return;
+      }
+      const uint32_t bytes = uint32_t(t.ntok) * 256;
+      pk_expect(&sm.vfull[st], bytes);
+      bulk_g2s(sm.vs[st].v, a.v[t.kind] + t.src_row * 128, bytes, &sm.vfull[st]);
+    };
+    int issued = 0;
+    for (; issued < min(kWsVStages, count); ++issued) load(issued);
+    int j = 0;
+    for (; j < count; ++j) {
+      const int st = j % kWsVStages;
+      if (!pk_wait(&sm.vfull[st], uint32_t(j / kWsVStages) & 1u)) {
+        flag(a.status, PKV_ST_TIMEOUT);
+        break;
+      }
+      const WsVMeta vm = sm.vmeta[st];
+      if (!vm.bad) bulk_s2g(a.v_out + vm.drow * 128, sm.vs[st].v, uint32_t(vm.ntok) * 256);
+      // one group per tile (empty for a bad one), so the groups count tiles
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      if (j >= 1 && issued < count) {
+        // tile j - 1's store has read its slot: refill it
+        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        load(issued++);
+      }
+    }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    for (int i = j; i < issued; ++i)  // after a timeout: loads still in flight
+      pk_wait(&sm.vfull[i % kWsVStages], uint32_t(i / kWsVStages) & 1u);
+    return;
+  }
+
+  // ---- consumers: rotate K into the packed buffer, copy the positions
+  const int ctid = int(threadIdx.x) - 64;
+  const int ch = ctid & 15;
   const float2* ftab[4];
   int fcols[4], fsel[4];
 #pragma unroll
@@ -502,29 +631,22 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
     ftab[j] = tab ? reinterpret_cast<const float2*>(tab) + col : nullptr;
   }
   const int rope_mode = a.rope_mode;
-
-  int done = 0;
   for (int i = 0; i < count; ++i) {
-    const int st = i % kBulkStages;
-    const bool ok = pk_wait(&sm.full[st], uint32_t(i / kBulkStages) & 1u);
-    if (__syncthreads_or(!ok)) {  // block-uniform: every thread leaves together
-      if (threadIdx.x == 0) flag(a.status, PKV_ST_TIMEOUT);
+    const int st = i % kWsKStages;
+    if (!pk_wait(&sm.kfull[st], uint32_t(i / kWsKStages) & 1u)) {
+      if (ctid == 0) flag(a.status, PKV_ST_TIMEOUT);
       break;
     }
     const BulkTileMeta m = sm.meta[st];
     if (!m.bad) {
-      const BulkStage& sb = sm.st[st];
+      const WsKStage& sb = sm.ks[st];
       const int64_t drow = m.dst0 + m.tok0;
-      if (threadIdx.x == 0) {
-        bulk_s2g(a.v_out + drow * 128, sb.v, uint32_t(m.ntok) * 256);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      }
       const bool has_pos = a.pos[m.kind] != nullptr;
       const bool rope = a.rope && has_pos;
       const int64_t* gpos = has_pos ? a.pos[m.kind] + m.src_row * 3 : nullptr;
 #pragma unroll
-      for (int q = 0; q < (kBulkTok * 16) / kBulkThreads; ++q) {
-        const int r = (int(threadIdx.x) + kBulkThreads * q) >> 4;
+      for (int q = 0; q < (kBulkTok * 16) / kWsConsumers; ++q) {
+        const int r = (ctid + kWsConsumers * q) >> 4;
         if (r >= m.ntok) continue;
         uint4 kk = *reinterpret_cast<const uint4*>(sb.k + r * 128 + ch * 8);
         if (rope) {
@@ -535,7 +657,6 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
             pt = __ldg(gpos + r * 3); py = __ldg(gpos + r * 3 + 1); px = __ldg(gpos + r * 3 + 2);
           }
           if (m.tm >= 0) pt = m.tm;
-          // table rows of this token, clamped once per coordinate
           const int rt = clamp_row(pt, a.ft_rows), ry = clamp_row(py, a.fy_rows);
           const int rx = clamp_row(px, a.fx_rows);
           uint32_t w[4] = {kk.x, kk.y, kk.z, kk.w};
@@ -556,22 +677,12 @@ __global__ void __launch_bounds__(kBulkThreads) pack_bulk_kernel(PackArgs a, Pla
       }
       if (a.pos_out != nullptr && has_pos) {
         int64_t* dp = a.pos_out + drow * 3;
-        for (int e = threadIdx.x; e < m.ntok * 3; e += blockDim.x)
+        for (int e = ctid; e < m.ntok * 3; e += kWsConsumers)
           dp[e] = m.pos_in_smem ? sb.pos[e] : __ldg(gpos + e);
       }
     }
-    __syncthreads();  // every read of stage st is done
-    done = i + 1;
-    if (threadIdx.x == 0 && issued < count) {
-      // the V store of this stage must have read its shared memory
-      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      issue(issued++);
-    }
-  }
-  if (threadIdx.x == 0) {
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    // on a timeout, let this block's own copies land before shared memory goes
-    for (int i = done; i < issued; ++i) pk_wait(&sm.full[i % kBulkStages], uint32_t(i / kBulkStages) & 1u);
+    __syncwarp();
+    if (lane == 0) pk_arrive(&sm.kempty[st]);
   }
 }
 
@@ -624,32 +735,28 @@ bool pack_bulk_ok(const PackArgs& a, int n_seg) {
 }
 
 template <bool kPlanned>
-constexpr int bulk_smem_bytes() {
-  return int(sizeof(BulkSmem)) + 128 + (kPlanned ? int(sizeof(PlannedSmem)) + 128 : 0);
+constexpr int ws_smem_bytes() {
+  return int(sizeof(WsSmem)) + 128 + (kPlanned ? int(sizeof(PlannedSmem)) + 128 : 0);
 }
 
-// A persistent grid of exactly the resident blocks.
 template <bool kPlanned>
-int launch_bulk(const PackArgs& a, const PlanArgs& pa, cudaStream_t stream) {
+int launch_ws(const PackArgs& a, const PlanArgs& pa, cudaStream_t stream) {
   static std::mutex mu;
-  static int per_sm_cache[kMaxDevices] = {};
-  constexpr int smem = bulk_smem_bytes<kPlanned>();
-  const int per_sm = per_device_once(per_sm_cache, mu, [] {
-    int n = 0;
-    if (cudaFuncSetAttribute(pack_bulk_kernel<kPlanned>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pack_bulk_kernel<kPlanned>,
-                                                      kBulkThreads, smem) != cudaSuccess) {
-      cudaGetLastError();
-      return 0;
-    }
-    return n < 1 ? 1 : n;
-  });
-  if (per_sm <= 0) return PKV_ELAUNCH;
-  pack_bulk_kernel<kPlanned><<<sm_count() * per_sm, kBulkThreads, smem, stream>>>(a, pa);
+  static int attr_done[kMaxDevices] = {};
+  constexpr int smem = ws_smem_bytes<kPlanned>();
+  if (per_device_once(attr_done, mu, [] {
+        return cudaFuncSetAttribute(pack_ws_kernel<kPlanned>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    smem) == cudaSuccess ? 1 : 0;
+      }) <= 0) {
+    cudaGetLastError();
+    return PKV_ELAUNCH;
+  }
+  pack_ws_kernel<kPlanned><<<sm_count(), kWsThreads, smem, stream>>>(a, pa);
   return launch_status();
 }
 
+// A persistent grid of exactly the resident blocks.
 }  // namespace
 
 int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, const int32_t* sl,
@@ -664,7 +771,7 @@ int launch_pack(const pkv_cache_t* c, const int32_t* sk, const int32_t* sg, cons
   a.n_seg = n_seg;
   a.tremap = tremap;
   a.rope = tremap != nullptr && (ft != nullptr || fy != nullptr || fx != nullptr);
-  if (pack_bulk_ok(a, n_seg)) return launch_bulk<false>(a, PlanArgs{}, stream);
+  if (pack_bulk_ok(a, n_seg)) return launch_ws<false>(a, PlanArgs{}, stream);
   const int max_len = a.F > a.MTPA ? a.F : a.MTPA;
   const int64_t units = int64_t(n_seg) * ((max_len + kPackTile - 1) / kPackTile);
   int64_t grid = int64_t(sm_count()) * 8;
@@ -699,7 +806,7 @@ int launch_pack_planned(const pkv_cache_t* c, const PlanArgs& pa, const float* f
   if (!plan_pack_fits(c, pa)) return PKV_EINVAL;
   PackArgs a = pack_args(c, ft, ft_rows, ft_cols, fy, fy_rows, fy_cols, fx, fx_rows, fx_cols);
   a.rope = ft != nullptr || fy != nullptr || fx != nullptr;
-  return launch_bulk<true>(a, pa, stream);
+  return launch_ws<true>(a, pa, stream);
 }
 
 }  // namespace pkv
