@@ -673,7 +673,8 @@ def run_head_parallel_line(args, rank: int, world: int, local: int):
                            f"{world // n} video(s)"),
             "us_per_layer_step": res["us_per_layer_step"], "head_parallel": res,
             "e2e": res.get("e2e"), "clocks": res["clocks"],
-            "gpu_launches": layer_steps(args.frames) * args.steps * 7,
+            # per layer-step: exchange in, route + copy, attend, exchange out
+            "gpu_launches": layer_steps(args.frames) * args.steps * (4 + attend_launches()),
             "device_status": res["device_status"]}
     print(json.dumps(line), flush=True)
 
@@ -773,7 +774,7 @@ def run_ours(args, rank: int, world: int, local: int):
     pack_bytes = tokens * (2 * D_ * 2 * 2 + 3 * 8 * 2)
     has_merge = bool(w.ctx.has_merge_head)
     clean_steps = n_ls // len(PASSES)
-    launches_per_video = n_ls * (2 + 3) + (clean_steps if has_merge else 0)
+    launches_per_video = n_ls * (2 + attend_launches()) + (clean_steps if has_merge else 0)
     e2e = None if args.no_e2e else e2e_videos(w, args, world)
     fps = world * args.steps * args.frames / (ms_max / 1e3)
     line = {
@@ -814,8 +815,8 @@ def run_ours(args, rank: int, world: int, local: int):
                             (upd / n_total / 1e3) / 1e9 / float(peaks["hbm_gbs"]),
                             "bytes_per_layer_step": update_algorithmic_bytes(w.labels,
                                                                              args.frames),
-                            "kernels": "route_kernel + copy_kernel (+ merge_kernel on clean "
-                                       "passes with merge heads)"},
+                            "kernels": "route_kernel + copy_kernel (+ merge_grid_kernel on "
+                                       "clean passes with merge heads)"},
         "kv_tokens_per_layer_step": tokens / n_total,
         "e2e": e2e,
         "gpu_launches": launches_per_video * args.steps,
@@ -894,6 +895,13 @@ def run_attn_c4(args):
         "flop_per_layer": sum(flops) / L_,
         "workload": "configs[3]: Q 4680/head, 12 heads, Lk ~ U{3..21} frames x 1560, "
                     "30 layers, bf16, N(0,1) K/V"}), flush=True)
+
+
+def attend_launches() -> int:
+    """Launches of one MegaCache.attend at the C2 shape: the pack that plans
+    for itself and the attention, or planner + pack + attention when
+    PKV_FUSED_PLAN_PACK=0 keeps the planner a launch of its own."""
+    return 3 if os.environ.get("PKV_FUSED_PLAN_PACK", "1").startswith("0") else 2
 
 
 def run_kernel_case(args):

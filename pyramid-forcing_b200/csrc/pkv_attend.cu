@@ -138,7 +138,8 @@ extern "C" int pkv_attend(const pkv_cache_t* c, const uint8_t* states_layer, int
 // library only the cache and each call's inputs and outputs, and a serving
 // loop cannot afford a cudaMalloc, which may synchronise the device and stall
 // the other streams.  The only scratch pkv_attend needs beyond the cache's own
-// buffers is the planner's descriptor arrays; here they live in the
+// buffers is the planner's descriptor arrays (for shapes the self-planning
+// pack does not cover; otherwise just the token total); here they live in the
 // file-scope array below, which every GPU that loads libpkv.so holds until the
 // process exits, and cache->scratch is not used (it may be NULL).
 //
@@ -210,14 +211,25 @@ extern "C" int pkv_attend_noalloc(const pkv_cache_t* c, const uint8_t* states_la
   int64_t ts[PKV_MAX_CHUNKS];
   for (int i = 0; i < num_chunks; ++i) ts[i] = first_t + i;
   auto s = static_cast<cudaStream_t>(stream);
-  int rc = launch_plan(c, states_layer, layer, ts, num_chunks, sink_mode, cmin, cmax, lag,
-                       /*check_capacity=*/1, /*add_layer_offset=*/1, c->cu_seqlens_k, sk, sg,
-                       sln, dst, traw, tremap, total, token_counter, s,
-                       c->first_t_dev);
-  if (rc != PKV_OK) return rc;
-  const bool rope = ft != nullptr || fy != nullptr || fx != nullptr;
-  rc = launch_pack(c, sk, sg, sln, dst, int(n), rope ? tremap : nullptr, ft, ft_rows, ft_cols,
-                   fy, fy_rows, fy_cols, fx, fx_rows, fx_cols, s);
+  int rc = PKV_OK;
+  if (!c->valid_count || !c->merge_token_count) return PKV_EINVAL;
+  if (layer < 0 || layer >= c->num_layers) return PKV_EINVAL;
+  const PlanArgs pa = plan_args(c, states_layer, layer, ts, num_chunks, sink_mode, cmin, cmax,
+                                lag, /*check_capacity=*/1, /*add_layer_offset=*/1,
+                                c->cu_seqlens_k, total, token_counter, c->first_t_dev);
+  if (fused_plan_pack() && plan_pack_fits(c, pa)) {
+    // the pack plans for itself: only the token total lands in the array
+    rc = launch_pack_planned(c, pa, ft, ft_rows, ft_cols, fy, fy_rows, fy_cols, fx, fx_rows,
+                             fx_cols, s);
+  } else {
+    rc = launch_plan(c, states_layer, layer, ts, num_chunks, sink_mode, cmin, cmax, lag,
+                     /*check_capacity=*/1, /*add_layer_offset=*/1, c->cu_seqlens_k, sk, sg,
+                     sln, dst, traw, tremap, total, token_counter, s, c->first_t_dev);
+    if (rc != PKV_OK) return rc;
+    const bool rope = ft != nullptr || fy != nullptr || fx != nullptr;
+    rc = launch_pack(c, sk, sg, sln, dst, int(n), rope ? tremap : nullptr, ft, ft_rows, ft_cols,
+                     fy, fy_rows, fy_cols, fx, fx_rows, fx_cols, s);
+  }
   if (rc != PKV_OK) return rc;
   // one CTA per attention unit: the split-unit workspace would be scratch
   return attend_attention(c, q, q_tok_stride, q_head_stride, num_chunks, scale, out,
