@@ -196,6 +196,21 @@ int pkv_plan(const pkv_cache_t *cache, const uint8_t *states_layer, int layer_id
              int64_t *total_tokens, int64_t *token_counter, pkv_stream_t stream);
 
 /*
+ * Legacy all-layer plan: per (layer, head) the descriptors of its sink,
+ * recent and middle segments (in that order), each from the head's slot 0
+ * over valid_count[kind] frames, or kind -1 when the kind is empty; offsets
+ * head-major over all layers.
+ * Replaces: adahead::pyramidkv_plan (pyramidkv/csrc/pyramidkv_plan.cc:48-173),
+ * op pyramidkv_plan (M1.4), which builds them on the host.
+ * Outputs (device int32): cu_seqlens_k [L*H+1]; src_kind, src_slot_global,
+ * seg_lengths, dst_token_offsets [L*H*3].  Segments may span several slots:
+ * pkv_pack copies them whole (they stay inside the pool).
+ */
+int pkv_legacy_plan(const pkv_cache_t *cache, int32_t *cu_seqlens_k, int32_t *src_kind,
+                    int32_t *src_slot_global, int32_t *seg_lengths,
+                    int32_t *dst_token_offsets, pkv_stream_t stream);
+
+/*
  * Gather pool segments into the flat K/V/pos workspace, rotating K by the 3D
  * RoPE at (tremap >= 0 ? tremap : stored t, stored y, stored x).
  * Replaces: adahead::launch_pyramidkv_pack

@@ -534,6 +534,38 @@ def legacy_write_frames(k_seq, v_seq, pos_seq, frame_desc, store_k, store_v, sto
         store_pos[slot] = pos_seq[src_frame * F:(src_frame + 1) * F]
 
 
+def legacy_plan(vc, F: int, max_sink: int, max_middle: int, max_recent: int):
+    """The M1.4 all-layer plan (pyramidkv_plan.cc:48-173): vc [L, H, 3] int64
+    valid counts -> (cu [L*H+1], sk, sg, sl, dst [L*H*3]) int32.  Per (layer,
+    head) the kinds sink (0), recent (2), middle (1) in that order; an active
+    kind is one segment from the head's slot 0 over valid_count frames, an
+    inactive one kind -1 with zero slot, length and offset."""
+    vc = np.asarray(vc, dtype=np.int64)
+    L, H = vc.shape[:2]
+    n = L * H
+    max_slots = (max_sink, max_middle, max_recent)
+    cu = np.zeros(n + 1, np.int32)
+    sk = np.full(n * 3, -1, np.int32)
+    sg = np.zeros(n * 3, np.int32)
+    sl = np.zeros(n * 3, np.int32)
+    dst = np.zeros(n * 3, np.int32)
+    run = 0
+    for i in range(n):
+        layer, head = divmod(i, H)
+        for kp, kind in enumerate((0, 2, 1)):
+            nv = int(vc[layer, head, kind])
+            if nv <= 0:
+                continue
+            d = i * 3 + kp
+            sk[d] = kind
+            sg[d] = i * max_slots[kind]
+            sl[d] = nv * F
+            dst[d] = run
+            run += nv * F
+        cu[i + 1] = run
+    return cu, sk, sg, sl, dst
+
+
 # ---------------------------------------------------------------------------
 # Query RoPE (wan/modules/causal_model.py:30-63)
 # ---------------------------------------------------------------------------

@@ -763,10 +763,6 @@ Tensor op_rope_q(Tensor x, Tensor ft, Tensor fy, Tensor fx, int64_t start_frame,
 int64_t op_status(Mgr mgr) { return take_status(mgr); }
 int64_t op_rope_rounding(int64_t mode) { return pkv_set_rope_rounding(int(mode)); }
 
-void unsupported_legacy(const char* name) {
-  TORCH_CHECK(false, name, " belongs to the AdaptiveKVCache / CppStrategyManager path, which "
-              "this library does not build; the MegaCache path does not call it");
-}
 // ---- AdaptiveKVCache / CppStrategyManager ops (scatter_copy_bind.cpp:449-684) ----
 void check_i64_1d(const Tensor& t, const char* name, int64_t n, const Tensor& like) {
   TORCH_CHECK(t.is_cuda() && t.dtype() == at::kLong && t.dim() == 1 && t.is_contiguous(),
@@ -910,9 +906,21 @@ void anchor_store_write_frames(Tensor k_seq, Tensor v_seq, Tensor pos_seq, Tenso
                store_k.size(2) * int64_t(store_k.element_size()), int(n), stream_of(store_k)),
            "anchor_store_write_frames");
 }
-std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> pyramidkv_plan(Mgr, int64_t, int64_t) {
-  unsupported_legacy("pyramidkv_plan");
-  return {};
+// pyramidkv_plan.cc:48-173: current_t and pass_kind are accepted and unused,
+// as there; the five descriptor tensors are new device tensors.
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> pyramidkv_plan(Mgr mgr, int64_t, int64_t) {
+  TORCH_CHECK(mgr.get() != nullptr, "pyramidkv_plan: manager is null");
+  const int64_t n = mgr->num_layers() * mgr->num_heads();
+  auto i32 = at::TensorOptions().dtype(at::kInt).device(mgr->device());
+  Tensor cu = at::empty({n + 1}, i32), sk = at::empty({n * 3}, i32), sg = at::empty({n * 3}, i32);
+  Tensor sl = at::empty({n * 3}, i32), dst = at::empty({n * 3}, i32);
+  c10::cuda::CUDAGuard g(mgr->device());
+  auto c = mgr->view();
+  check_rc(pkv_legacy_plan(&c, cu.data_ptr<int32_t>(), sk.data_ptr<int32_t>(),
+                           sg.data_ptr<int32_t>(), sl.data_ptr<int32_t>(),
+                           dst.data_ptr<int32_t>(), stream_of(cu)),
+           "pyramidkv_plan");
+  return {cu, sk, sg, sl, dst};
 }
 
 // ---- Meta kernels (shape-only) ----

@@ -93,8 +93,7 @@ __global__ void __launch_bounds__(256) pack_kernel(PackArgs a) {
     const int kind = a.sk[seg];
     if (kind < 0) continue;
     const int len = a.sl[seg];
-    const int tok0 = tile * kPackTile;
-    if (len <= 0 || tok0 >= len) continue;
+    if (len <= 0 || tile * kPackTile >= len) continue;
     if (kind > 3) {
       if (tile == 0 && threadIdx.x == 0) flag(a.status, PKV_ST_BAD_KIND);
       continue;
@@ -102,13 +101,15 @@ __global__ void __launch_bounds__(256) pack_kernel(PackArgs a) {
     const int64_t slot = a.sg[seg];
     const int64_t dst0 = a.dst[seg];
     const int stride_tok = kind == kSrcMerge ? a.MTPA : a.F;
-    if (slot < 0 || slot >= a.rows[kind] || len > stride_tok || dst0 < 0 ||
+    // a segment may span consecutive slots (the legacy all-layer plan) but
+    // must stay inside its pool
+    if (slot < 0 || slot >= a.rows[kind] ||
+        slot * stride_tok + len > a.rows[kind] * stride_tok || dst0 < 0 ||
         dst0 + len > a.out_rows || a.k[kind] == nullptr) {
       if (tile == 0 && threadIdx.x == 0)
         flag(a.status, dst0 + len > a.out_rows ? PKV_ST_PACK_OVERFLOW : PKV_ST_SLOT_RANGE);
       continue;
     }
-    const int ntok = min(kPackTile, len - tok0);
     const int D = a.D;
     const uint16_t* sk = a.k[kind] + slot * stride_tok * D;
     const uint16_t* sv = a.v[kind] + slot * stride_tok * D;
@@ -118,57 +119,62 @@ __global__ void __launch_bounds__(256) pack_kernel(PackArgs a) {
     const bool rope = a.rope && sp != nullptr;
     const int64_t tm = rope ? a.tremap[seg] : -1;
 
-    if (kVec) {
-      const int cpr = D / 8;
-      for (int i = threadIdx.x; i < ntok * cpr; i += blockDim.x) {
-        const int r = i / cpr, ch = i - r * cpr;
-        const int64_t e = int64_t(tok0 + r) * D + ch * 8;
-        uint4 kk = *reinterpret_cast<const uint4*>(sk + e);
-        const uint4 vv = *reinterpret_cast<const uint4*>(sv + e);
-        if (rope) {
-          const int64_t* pp = sp + int64_t(tok0 + r) * 3;
-          const int64_t pt = tm >= 0 ? tm : pp[0];
-          const int64_t py = pp[1], px = pp[2];
-          uint32_t w[4] = {kk.x, kk.y, kk.z, kk.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 fq = freq_of(a, ch * 4 + j, pt, py, px);
-            const float kr = bf16_bits_to_f32(w[j] & 0xffffu);
-            const float ki = bf16_bits_to_f32(w[j] >> 16);
-            float nr, ni;
-            rotate(kr, ki, fq.x, fq.y, a.rope_mode, nr, ni);
-            w[j] = f32_to_bf16_bits(nr) | (f32_to_bf16_bits(ni) << 16);
+    // a unit takes tiles tile, tile + tiles, ... of its segment (a legacy
+    // all-layer plan's segment spans several slots)
+    for (int tok0 = tile * kPackTile; tok0 < len; tok0 += tiles * kPackTile) {
+      const int ntok = min(kPackTile, len - tok0);
+      if (kVec) {
+        const int cpr = D / 8;
+        for (int i = threadIdx.x; i < ntok * cpr; i += blockDim.x) {
+          const int r = i / cpr, ch = i - r * cpr;
+          const int64_t e = int64_t(tok0 + r) * D + ch * 8;
+          uint4 kk = *reinterpret_cast<const uint4*>(sk + e);
+          const uint4 vv = *reinterpret_cast<const uint4*>(sv + e);
+          if (rope) {
+            const int64_t* pp = sp + int64_t(tok0 + r) * 3;
+            const int64_t pt = tm >= 0 ? tm : pp[0];
+            const int64_t py = pp[1], px = pp[2];
+            uint32_t w[4] = {kk.x, kk.y, kk.z, kk.w};
+  #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 fq = freq_of(a, ch * 4 + j, pt, py, px);
+              const float kr = bf16_bits_to_f32(w[j] & 0xffffu);
+              const float ki = bf16_bits_to_f32(w[j] >> 16);
+              float nr, ni;
+              rotate(kr, ki, fq.x, fq.y, a.rope_mode, nr, ni);
+              w[j] = f32_to_bf16_bits(nr) | (f32_to_bf16_bits(ni) << 16);
+            }
+            kk = make_uint4(w[0], w[1], w[2], w[3]);
           }
-          kk = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(dk + e) = kk;
+          *reinterpret_cast<uint4*>(dv + e) = vv;
         }
-        *reinterpret_cast<uint4*>(dk + e) = kk;
-        *reinterpret_cast<uint4*>(dv + e) = vv;
-      }
-    } else {
-      const int ppr = D / 2;
-      for (int i = threadIdx.x; i < ntok * ppr; i += blockDim.x) {
-        const int r = i / ppr, p = i - r * ppr;
-        const int64_t e = int64_t(tok0 + r) * D + p * 2;
-        uint16_t k0 = sk[e], k1 = sk[e + 1];
-        if (rope) {
-          const int64_t* pp = sp + int64_t(tok0 + r) * 3;
-          const int64_t pt = tm >= 0 ? tm : pp[0];
-          const float2 fq = freq_of(a, p, pt, pp[1], pp[2]);
-          float nr, ni;
-          rotate(bf16_bits_to_f32(k0), bf16_bits_to_f32(k1), fq.x, fq.y, a.rope_mode, nr, ni);
-          k0 = static_cast<uint16_t>(f32_to_bf16_bits(nr));
-          k1 = static_cast<uint16_t>(f32_to_bf16_bits(ni));
+      } else {
+        const int ppr = D / 2;
+        for (int i = threadIdx.x; i < ntok * ppr; i += blockDim.x) {
+          const int r = i / ppr, p = i - r * ppr;
+          const int64_t e = int64_t(tok0 + r) * D + p * 2;
+          uint16_t k0 = sk[e], k1 = sk[e + 1];
+          if (rope) {
+            const int64_t* pp = sp + int64_t(tok0 + r) * 3;
+            const int64_t pt = tm >= 0 ? tm : pp[0];
+            const float2 fq = freq_of(a, p, pt, pp[1], pp[2]);
+            float nr, ni;
+            rotate(bf16_bits_to_f32(k0), bf16_bits_to_f32(k1), fq.x, fq.y, a.rope_mode, nr, ni);
+            k0 = static_cast<uint16_t>(f32_to_bf16_bits(nr));
+            k1 = static_cast<uint16_t>(f32_to_bf16_bits(ni));
+          }
+          dk[e] = k0;
+          dk[e + 1] = k1;
+          dv[e] = sv[e];
+          dv[e + 1] = sv[e + 1];
         }
-        dk[e] = k0;
-        dk[e + 1] = k1;
-        dv[e] = sv[e];
-        dv[e + 1] = sv[e + 1];
       }
-    }
-    if (a.pos_out != nullptr && sp != nullptr) {
-      int64_t* dp = a.pos_out + dst0 * 3;
-      for (int e = threadIdx.x; e < ntok * 3; e += blockDim.x)
-        dp[int64_t(tok0) * 3 + e] = sp[int64_t(tok0) * 3 + e];
+      if (a.pos_out != nullptr && sp != nullptr) {
+        int64_t* dp = a.pos_out + dst0 * 3;
+        for (int e = threadIdx.x; e < ntok * 3; e += blockDim.x)
+          dp[int64_t(tok0) * 3 + e] = sp[int64_t(tok0) * 3 + e];
+      }
     }
   }
 }
@@ -434,7 +440,10 @@ __device__ __forceinline__ PackTile pack_tile(const PackArgs& a, const PlanArgs&
   t.tok0 = (u - tile_start[iseg]) * kBulkTok;
   t.ntok = min(kBulkTok, len - t.tok0);
   t.dst0 = dst0;
-  t.bad = slot < 0 || slot >= a.rows[kind] || len > stride_tok || dst0 < 0 ||
+  // a segment may span consecutive slots (the legacy all-layer plan) but
+  // must stay inside its pool
+  t.bad = slot < 0 || slot >= a.rows[kind] ||
+          slot * stride_tok + len > a.rows[kind] * stride_tok || dst0 < 0 ||
           dst0 + len > a.out_rows || a.k[kind] == nullptr;
   t.src_row = slot * stride_tok + t.tok0;
   t.tm = (a.rope && a.pos[kind] != nullptr) ? seg_tremap : -1;

@@ -327,6 +327,85 @@ int launch_plan(const pkv_cache_t* c, const uint8_t* states_layer, int layer,
   return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Legacy all-layer plan (the M1.4 op pyramidkv_plan, pyramidkv_plan.cc:48-173):
+// every (layer, head) emits three descriptors in the order sink, recent,
+// middle; an active kind (valid_count > 0) is one segment from the head's
+// slot 0 spanning valid_count frames (slots assumed filled 0..n-1), an
+// inactive one kind -1 with zero slot, length and offset.  Offsets run
+// head-major through all layers; cu_seqlens_k has one entry per (layer,
+// head).  The reference builds this on the host from a blocking copy of
+// valid_count and copies five arrays back; here one CTA scans the heads'
+// totals (1024 per round, carried between rounds) on the device.
+// ---------------------------------------------------------------------------
+constexpr int kLegacyPlanThreads = 1024;
+
+__global__ void __launch_bounds__(kLegacyPlanThreads) legacy_plan_kernel(
+    const int64_t* __restrict__ vc, int N, int F, int max_sink, int max_middle,
+    int max_recent, int32_t* __restrict__ cu, int32_t* __restrict__ sk,
+    int32_t* __restrict__ sg, int32_t* __restrict__ sl, int32_t* __restrict__ dst) {
+  __shared__ int32_t warp_sum[kLegacyPlanThreads / 32];
+  __shared__ int32_t carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kind_order[3] = {0, 2, 1};  // sink, recent, middle
+  const int max_slots[3] = {max_sink, max_middle, max_recent};
+  if (tid == 0) {
+    carry = 0;
+    cu[0] = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < N; base += blockDim.x) {
+    const int i = base + tid;
+    int32_t len[3] = {0, 0, 0};
+    int32_t tot = 0;
+    if (i < N) {
+#pragma unroll
+      for (int kp = 0; kp < 3; ++kp) {
+        const int64_t n = vc[int64_t(i) * 3 + kind_order[kp]];
+        len[kp] = n > 0 ? static_cast<int32_t>(n) * F : 0;
+        tot += len[kp];
+      }
+    }
+    int32_t incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sum[warp] = incl;
+    __syncthreads();
+    int32_t before = carry, round_total = 0;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) {
+      if (w < warp) before += warp_sum[w];
+      round_total += warp_sum[w];
+    }
+    if (i < N) {
+      int32_t run = before + incl - tot;
+#pragma unroll
+      for (int kp = 0; kp < 3; ++kp) {
+        const int kind = kind_order[kp];
+        const int64_t d = int64_t(i) * 3 + kp;
+        if (len[kp] <= 0) {
+          sk[d] = -1;
+          sg[d] = 0;
+          sl[d] = 0;
+          dst[d] = 0;
+          continue;
+        }
+        sk[d] = kind;
+        sg[d] = i * max_slots[kind];  // (layer * H + head) * max_slots + slot 0
+        sl[d] = len[kp];
+        dst[d] = run;
+        run += len[kp];
+      }
+      cu[i + 1] = run;
+    }
+    __syncthreads();
+    if (tid == 0) carry += round_total;
+    __syncthreads();
+  }
+}
+
 }  // namespace pkv
 
 using namespace pkv;
@@ -344,4 +423,19 @@ extern "C" int pkv_plan(const pkv_cache_t* c, const uint8_t* states_layer, int l
                      add_layer_offset, cu_seqlens_k, src_kind, src_slot_global, seg_lengths,
                      dst_token_offsets, anchor_t_raw, anchor_t_remap, total_tokens,
                      token_counter, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" int pkv_legacy_plan(const pkv_cache_t* c, int32_t* cu_seqlens_k, int32_t* src_kind,
+                               int32_t* src_slot_global, int32_t* seg_lengths,
+                               int32_t* dst_token_offsets, pkv_stream_t stream) {
+  if (!c || !c->valid_count || !cu_seqlens_k || !src_kind || !src_slot_global || !seg_lengths ||
+      !dst_token_offsets)
+    return PKV_EINVAL;
+  const int64_t n = int64_t(c->num_layers) * c->num_heads;
+  if (n <= 0) return PKV_EINVAL;
+  if (n > (int64_t(1) << 28)) return PKV_ECAPACITY;
+  legacy_plan_kernel<<<1, kLegacyPlanThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      c->valid_count, int(n), c->frame_seqlen, c->max_sink, c->max_middle, c->max_recent,
+      cu_seqlens_k, src_kind, src_slot_global, seg_lengths, dst_token_offsets);
+  return launch_status();
 }
