@@ -734,7 +734,7 @@ bool pack_vec_ok(const PackArgs& a) {
   return vec;
 }
 
-// The bulk kernel's 16-byte rules: head_dim 128, every pool and output
+// The head_dim-128 pack's 16-byte rules: head_dim 128, every pool and output
 // 16-byte aligned, the segment list within the kernel's tile table.
 bool pack_bulk_ok(const PackArgs& a, int n_seg) {
   return pack_vec_ok(a) && a.D == 128 && n_seg <= kPack128MaxSeg &&
