@@ -121,6 +121,43 @@ def test_megacache_blocks_match_oracle(cuda, routing, W, Hgrid):
     assert orc.mtc.max() > 0 or routing == "yaml"
 
 
+@pytest.mark.parametrize("F", [1, 4])
+def test_megacache_frames_per_call(cuda, F):
+    """Updates of 1 and 4 frames per call (the model's blocks have 3): the
+    merge kernel takes a call's frames in batches of 3, the pack plans F
+    chunks.  State, pools, accumulators and packed K/V bit-exact."""
+    rng = np.random.default_rng(23 + F)
+    labels = np.array([[-1, 1, 2, -1]])
+    W, Hgrid = 13, 8
+    caches, orc = _build(cuda, labels, "baseline", W, Hgrid)
+    L, H = labels.shape
+    D, FSEQ = 128, W * Hgrid
+    for blk in range(12 if F == 1 else 6):
+        start = blk * F * FSEQ
+        for mode in ("noisy", "clean"):
+            k = O.f32_to_bf16(rng.standard_normal((1, F * FSEQ, H, D)).astype(np.float32))
+            v = O.f32_to_bf16(rng.standard_normal((1, F * FSEQ, H, D)).astype(np.float32))
+            q = O.f32_to_bf16(rng.standard_normal((1, F * FSEQ, H, D)).astype(np.float32))
+            orc.update(0, k, v, start, mode)
+            caches[0].update(_bf16(k, cuda).view(1, -1, H, D), _bf16(v, cuda).view(1, -1, H, D),
+                             start, cache_update_mode=mode)
+            want, pk = orc.attend(0, q, start)
+            got = caches[0].attend(_bf16(q, cuda).view(1, -1, H, D), start)
+            torch.cuda.synchronize()
+            where = f"F={F} block {blk} {mode}"
+            _compare_state(caches[0], orc, 0, where)
+            mgr = caches[0].ctx.mgr
+            total = pk["total"]
+            np.testing.assert_array_equal(mgr.cu_seqlens_k()[:F * H + 1].cpu().numpy(), pk["cu"],
+                                          err_msg=where)
+            np.testing.assert_array_equal(_u16(mgr.k_flat_out()[:total]).reshape(total, D),
+                                          pk["k"], err_msg=f"{where}: packed K")
+            err = (got.float().cpu().numpy() - want).__abs__()
+            assert err.max() <= 2e-2 and err.mean() <= 2e-3, (where, err.max(), err.mean())
+    assert caches[0].ctx.check_status() == 0
+    assert orc.mtc.max() > 0
+
+
 def test_update_rejects_bad_shapes(cuda):
     caches, _ = _build(cuda, np.array([[1, 2]]), "baseline", 13, 8)
     with pytest.raises((AssertionError, RuntimeError)):
