@@ -84,10 +84,14 @@ def _mgr(L, H, D, F, ms, mm, mr, mac=4):
 
 
 @pytest.mark.parametrize("sink_mode", ["lag", "window_clamp"])
-def test_plan_multi_bit_exact(cuda, sink_mode):
+@pytest.mark.parametrize("ms,mm,mr", [(3, 24, 4), (5, 24, 6)])
+def test_plan_multi_bit_exact(cuda, sink_mode, ms, mm, mr):
+    """(3, 24, 4): the warp-per-(chunk, head) planner; (5, 24, 6): more sink
+    and recent slots than its candidate list holds, the thread-per-(chunk,
+    head) planner (plan_kernel)."""
     from pyramidkv import _mega_state_ops as so
     rng = np.random.default_rng(3)
-    L, H, D, F, ms, mm, mr = 3, len(MIX), 16, 8, 3, 24, 4
+    L, H, D, F = 3, len(MIX), 16, 8
     mgr = _mgr(L, H, D, F, ms, mm, mr)
     for trial in range(6):
         st, t_end = _states_after(rng, MIX, steps=int(rng.integers(1, 25)))
