@@ -158,6 +158,37 @@ def test_megacache_frames_per_call(cuda, F):
     assert orc.mtc.max() > 0
 
 
+def test_self_planning_pack_bounds_checks_corrupt_counts(cuda):
+    """Merge token counts far past an anchor's capacity (a corrupted manager):
+    the pack that plans for itself must flag the segments (pack overflow, slot
+    range) and skip them, not read or write out of bounds, and attend raises
+    the reference's capacity error; the cache keeps working once the counts
+    are sane again."""
+    labels = np.array([[-1, -1, 1, 2]])
+    caches, orc = _build(cuda, labels, "baseline", 13, 8)
+    H, D, FSEQ, F = 4, 128, 13 * 8, 3
+    rng = np.random.default_rng(5)
+    mk = lambda: _bf16(O.f32_to_bf16(rng.standard_normal((1, F * FSEQ, H, D))  # noqa: E731
+                                     .astype(np.float32)), cuda).view(1, -1, H, D)
+    for blk in range(6):
+        caches[0].update(mk(), mk(), blk * F * FSEQ, cache_update_mode="clean")
+    caches[0].attend(mk(), 6 * F * FSEQ)
+    assert caches[0].ctx.check_status() == 0
+    mtc = caches[0].ctx.mgr.merge_token_count()
+    assert int(mtc.max()) > 0, "no merge anchor was finalized"
+    saved = mtc.clone()
+    mtc.masked_fill_(mtc > 0, 60000)
+    # the reference's planner raises on a plan past the workspace; the op
+    # reads the device's overflow bit (and clears the status word) to do so
+    with pytest.raises(RuntimeError, match="exceed pack-workspace capacity"):
+        caches[0].attend(mk(), 6 * F * FSEQ)
+    mtc.copy_(saved)
+    out = caches[0].attend(mk(), 6 * F * FSEQ)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    assert caches[0].ctx.check_status() == 0
+
+
 def test_update_rejects_bad_shapes(cuda):
     caches, _ = _build(cuda, np.array([[1, 2]]), "baseline", 13, 8)
     with pytest.raises((AssertionError, RuntimeError)):
