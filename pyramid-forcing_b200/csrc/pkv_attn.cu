@@ -325,7 +325,7 @@ struct AttnArgs {
 // q_empty commit after a piece's last Q·K^T lets the next piece's Q load.
 // The first P·V of a piece (which overwrites O_t) waits for P_t of that
 // piece, which the softmax warps post only after reading O_t of the last one.
-// Softmax: exp2 of 2 of every 5 column pairs on the FMA pipe (exp2_poly2),
+// Softmax: exp2 of 3 of every 16 column pairs on the FMA pipe (exp2_poly2),
 // the rest on MUFU; the last (partial) K tile uses MUFU only, which maps the
 // masked -inf scores to exactly 0.
 // ---------------------------------------------------------------------------
@@ -375,8 +375,12 @@ __device__ __forceinline__ float row_max128(const uint32_t (&s)[4][32]) {
   return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
-// Which column pairs of a 32-column chunk take the FMA-pipe exp2: 6 of 16.
-__host__ __device__ constexpr bool poly_pair(int i) { return i % 5 == 1 || i % 5 == 3; }
+// Which column pairs of a 32-column chunk take the FMA-pipe exp2: 3 of 16
+// (pairs 2, 7, 12).  Measured on B200 (attention kernel case, one call):
+// 0.5245 ms with 3 of 16, 0.5263 with 4, 0.5284 with 2, 0.543 with 6, 0.567
+// with 8, and all on MUFU 1.4% slower than 6 of 16: the FMA / ALU side is
+// the more contended pipe.
+__host__ __device__ constexpr bool poly_pair(int i) { return i % 5 == 2; }
 
 // P for 32 columns (16 pairs) of one row: p = 2^(s * scale - m), summed into
 // two paired accumulators and packed to bf16 pairs.
