@@ -111,14 +111,21 @@ def bf16_to_f32(a: np.ndarray) -> np.ndarray:
 
 
 def f32_to_bf16(a: np.ndarray) -> np.ndarray:
-    """Round-to-nearest-even fp32 -> bf16 bits (finite inputs)."""
-    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    lsb = (u >> 16) & 1
-    r = ((u + 0x7FFF + lsb) >> 16).astype(np.uint16)
+    """Round-to-nearest-even fp32 -> bf16 bits; NaN -> 0x7FC0.  In 32-bit
+    arithmetic, in place: bits + 0x7FFF + lsb cannot pass 2^32 for any
+    finite or infinite input, and NaNs are overwritten."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32)
+    r = u >> 16
+    r &= 1
+    r += 0x7FFF
+    r += u
+    r >>= 16
+    out = r.astype(np.uint16)
     nan = np.isnan(a)
     if nan.any():
-        r = np.where(nan, np.uint16(0x7FC0), r)
-    return r
+        out[nan] = 0x7FC0
+    return out
 
 
 def state_size() -> int:
